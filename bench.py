@@ -1,0 +1,278 @@
+"""Benchmark of the B200 decode-step token sampler.
+
+Workload (BASELINE.json's headline): fp32 logits [4096 x 151,936] N(0, 2^2),
+temperature 0.8, top_k 50, one uniform per row -- the "throughput sweep"
+configuration at its largest single-GPU batch. A step samples every row once
+(one launch of the fused kernel). Inputs (2.49 GB per GPU) exceed the 126 MB L2,
+so no flush is needed between steps. Multi-GPU: rows are sharded across ranks
+with no communication (weak scaling: 4096 rows per GPU).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--rows B]
+
+--impl reference times the reference's own sampling block on the host cores
+(oracle/_ref, compiled from the reference's source; the restated oracle when
+that was not built) on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "minxfmr.cpp_b200"))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+V = 151936
+TEMPERATURE = 0.8
+TOP_K = 50
+SIGMA = 2.0
+METRIC = "sampled rows/s (V=151936 fp32, top_k 50)"
+UNIT = "rows/s"
+# ncu dram__bytes_read.sum + dram__bytes_write.sum of one sample_kernel launch
+# per row of this workload (profiles/sample_kernel_b4096_v151936.md); None until captured.
+NCU_TRAFFIC_BYTES_PER_ROW = None
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms."""
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_run(rows_sample, seconds, threads=0):
+    """Time the reference's sampling block (or the oracle port) on host cores.
+    Returns (rows/s, kind, cores, description)."""
+    import numpy as np
+    import oracle_lib
+    import workloads
+    if not os.path.exists(oracle_lib.ORACLE_SO):
+        oracle_lib.build()
+    x = workloads.normal(7, rows_sample, V, SIGMA)
+    u = oracle_lib.uniforms(7, rows_sample)
+    cores = threads if threads > 0 else (os.cpu_count() or 1)
+    kind = "reference" if oracle_lib.ref_available() else "port"
+
+    def one():
+        if kind == "reference":
+            oracle_lib.ref_sample(x, TEMPERATURE, TOP_K, 7, threads=cores)
+        else:
+            oracle_lib.oracle_sample(x, TEMPERATURE, TOP_K, u, threads=cores)
+
+    one()  # warm
+    done, t0 = 0, time.perf_counter()
+    while True:
+        one()
+        done += rows_sample
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    what = ("the reference's own sampling block (src/api/minxfmr.cpp:2091-2171, oracle/_ref)"
+            if kind == "reference" else "the oracle port of that block")
+    desc = (f"{what} on {done} rows ({rows_sample}-row batches of the same N(0,2^2) x 151936 workload, "
+            f"T=0.8, top_k 50) over {el:.1f} s, {cores} threads")
+    return done / el, kind, cores, desc
+
+
+def run_reference_arm(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return 0
+    rows_sample = 256
+    vals = []
+    for _ in range(args.warmup):
+        cpu_reference_run(rows_sample, 0.0)
+    for _ in range(args.steps):
+        v, kind, cores, desc = cpu_reference_run(rows_sample, 0.0)
+        vals.append(v)
+    value = statistics.median(vals)
+    ms = rows_sample / value * 1e3
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": f"c5 throughput: {rows_sample}-row sample per step of [4096 x {V}] fp32 "
+                                   f"N(0,2^2), T=0.8, top_k 50 (host cores)"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--rows", type=int, default=4096)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+    import mxs_sampler
+
+    rank, world, local = env_rank()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    rows = args.rows
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    logits = torch.randn((rows, V), generator=gen, device=dev, dtype=torch.float32) * SIGMA
+    u = torch.rand(rows, generator=gen, device=dev, dtype=torch.float64)
+    nxt = torch.empty(rows, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    out = (nxt, None, None, None)
+
+    def step():
+        mxs_sampler.sample(logits, TEMPERATURE, TOP_K, u, out=out, return_topk=False, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    with ClockSampler(gpu_index) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms_total = ev0.elapsed_time(ev1)
+        # keep the GPU under the same load ~1 s more so the clock record has samples
+        t_end = time.time() + 1.0
+        while time.time() < t_end:
+            for _ in range(50):
+                step()
+            torch.cuda.synchronize()
+    t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_step = ms_max / args.steps
+    value = world * rows * args.steps / (ms_max / 1e3)
+
+    # end to end through the host-buffer C-ABI entry: pinned logits in, ids out
+    e2e = None
+    if not args.no_e2e:
+        import numpy as np
+        h_logits = torch.empty((rows, V), dtype=torch.float32).pin_memory()
+        h_logits.copy_(logits.cpu())
+        h_u = u.cpu().pin_memory()
+        n_e2e = max(3, min(args.steps, 10))
+        mxs_sampler.sample_host(h_logits, TEMPERATURE, TOP_K, h_u)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            mxs_sampler.sample_host(h_logits, TEMPERATURE, TOP_K, h_u)
+        el = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(el, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * rows * n_e2e / float(el.item()), "unit": UNIT,
+               "h2d_bytes_per_step": rows * V * 4 + rows * 8, "d2h_bytes_per_step": rows * 4,
+               "steps": n_e2e, "timing": "host wall clock around synchronous calls (max over ranks)"}
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        bytes_per_launch = rows * V * 4
+        achieved = bytes_per_launch / (ms_total / args.steps / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs (burst copy)",
+                    "traffic": (NCU_TRAFFIC_BYTES_PER_ROW * rows) if NCU_TRAFFIC_BYTES_PER_ROW else None,
+                    "kernel": "mxs::sample_kernel<true>", "algorithmic_bytes_per_launch": bytes_per_launch}
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            v, kind, cores, desc = cpu_reference_run(256, args.cpu_seconds)
+            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc}
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (torch.randn seeded, N(0,2^2))",
+                "config": {"workload": f"c5 throughput: [{rows} x {V}] fp32 logits per GPU, T=0.8, top_k 50, "
+                                       "one uniform per row", "rows_per_gpu": rows, "vocab": V, "top_k": TOP_K,
+                           "temperature": TEMPERATURE, "parallelism": f"row-sharded x{world}, no collective",
+                           "l2": "inputs (2.49 GB per GPU) larger than L2; no flush"},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+                "hbm_frac_of_8tbs": achieved / 8000.0, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

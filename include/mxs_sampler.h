@@ -1,0 +1,148 @@
+/*
+ * mxs_sampler.h -- C ABI of the B200 (sm_100a) decode-step token sampler.
+ *
+ * The sampler replaces the sampling block of the reference's
+ * minxfmr_generate (src/api/minxfmr.cpp:2091-2171):
+ *
+ *   k_use = clamp(top_k)                       src/api/minxfmr.cpp:1567, :2091-2093
+ *   order = std::partial_sort top-k            src/api/minxfmr.cpp:2095-2102
+ *   greedy when temperature <= 0               src/api/minxfmr.cpp:1550, :2113-2115
+ *   p_i = exp((l_i - l_max) / T), normalise    src/api/minxfmr.cpp:2117-2126
+ *   top-p / min-p truncation                   src/api/minxfmr.cpp:2104-2111, :2128-2165
+ *   std::discrete_distribution draw            src/api/minxfmr.cpp:2167-2169
+ *
+ * for a batch of fp32 logits rows kept in device memory. Its results equal the
+ * reference block's on the same logits and the same uniform: the top-k index
+ * set and its tie order (the order libstdc++'s heap-based partial_sort leaves),
+ * the sampled token id, and the probabilities (same double operations, same
+ * order; exp is CUDA's double exp, within 1 ulp of glibc's).
+ *
+ * The reference draws u from a function-static std::mt19937
+ * (src/api/minxfmr.cpp:1568); here the caller passes one u in [0, 1) per row,
+ * which is what std::discrete_distribution draws (generate_canonical<double,53>)
+ * from the engine. Given the engine's u the pick is the same.
+ *
+ * Conventions (as the reference's C API, include/minxfmr.h:9-37): functions
+ * return 0 on success and a negative code on error; nothing throws. Device
+ * pointers are owned by the caller. Calls are asynchronous on `stream`
+ * (a cudaStream_t; NULL = legacy default stream) unless stated otherwise.
+ * No CPU fallback exists: without a usable sm_100 device every call returns
+ * MXS_ERR_NO_DEVICE.
+ */
+#ifndef MXS_SAMPLER_H
+#define MXS_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MXS_API __attribute__((visibility("default")))
+#else
+#define MXS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MXS_OK 0
+#define MXS_ERR_INVALID (-1)   /* bad argument (null pointer, rows < 0, vocab <= 0, ld < vocab) */
+#define MXS_ERR_CUDA (-3)      /* a CUDA call failed (cf. the reference's -3 for backend failures) */
+#define MXS_ERR_TIMEOUT (-4)   /* a bounded device wait gave up (see mxs_get_status) */
+#define MXS_ERR_NO_DEVICE (-5) /* no sm_100 device current */
+#define MXS_ERR_WORKSPACE (-6) /* caller workspace too small or misaligned */
+
+/* Per-row flag bits written to d_row_flags (optional). */
+#define MXS_ROW_EXACT 1u    /* the row had ties (or NaNs) and was resolved by the exact heap replay */
+#define MXS_ROW_NAN 2u      /* the row holds a NaN logit */
+#define MXS_ROW_OVERFLOW 4u /* candidate buffers overflowed (massive ties); exact replay used */
+#define MXS_ROW_TIMEOUT 8u  /* a bounded wait gave up; next[row] = -1 */
+
+/*
+ * Sample one token per row.
+ *   d_logits   rows x ld fp32 (row r at d_logits + r*ld), vocab <= ld valid columns
+ *   temperature, top_k   as minxfmr_generate: T <= 0 is greedy; top_k <= 0 means 1;
+ *              top_k > vocab means vocab
+ *   d_u        rows doubles in [0, 1): the uniform of each row's draw
+ *   d_next     rows int32: sampled token id
+ *   d_topk_idx rows x k_use int32 (nullable): the reference's order[0, k_use)
+ *   d_topk_prob rows x k_use double (nullable): p_i / sum (src/api/minxfmr.cpp:2123-2126);
+ *              greedy rows (T <= 0, or sum <= 0) get 1, 0, 0, ...
+ * Uses a library-owned workspace on the current device, allocated on the
+ * first call that needs more than the last (make that first call before any
+ * stream capture). Replaces src/api/minxfmr.cpp:2091-2171 (top_p = 1, min_p = 0).
+ */
+MXS_API int mxs_sample_topk(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
+                    int top_k, const double* d_u, int32_t* d_next, int32_t* d_topk_idx, double* d_topk_prob,
+                    void* stream);
+
+/*
+ * As mxs_sample_topk, plus top_p / min_p (clamped as src/api/minxfmr.cpp:2104-2111),
+ * optional per-row flags, and an optional caller workspace. With
+ * d_workspace == NULL the library-owned workspace is used; otherwise
+ * workspace_bytes must be >= mxs_workspace_size(...) and the workspace must
+ * have been zero-filled once (mxs_workspace_init); every call leaves it zeroed
+ * again for the next. Calls sharing one workspace must not overlap on the GPU.
+ */
+MXS_API int mxs_sample_topk_ex(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
+                       int top_k, double top_p, double min_p, const double* d_u, int32_t* d_next,
+                       int32_t* d_topk_idx, double* d_topk_prob, uint32_t* d_row_flags, void* d_workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace mxs_sample_topk_ex needs for this shape on the current device. */
+MXS_API int mxs_workspace_size(int64_t rows, int64_t vocab, int top_k, size_t* bytes);
+
+/* Zero-fill a caller workspace (once, before its first use). */
+MXS_API int mxs_workspace_init(void* d_workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Host-buffer entry point: the drop-in for a caller whose logits are on the
+ * host (the reference copies lm_head logits to the host, src/backend/cuda/
+ * cuda_backend.cu:1440-1442, and samples there). Copies logits and u to the
+ * device, samples, copies next (and the optional top-k outputs) back, and
+ * returns when they are in host memory. Pinned host buffers make the copies
+ * asynchronous DMA; pageable ones work too.
+ */
+MXS_API int mxs_sample_topk_host(const float* h_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
+                         int top_k, double top_p, double min_p, const double* h_u, int32_t* h_next,
+                         int32_t* h_topk_idx, double* h_topk_prob, void* stream);
+
+/*
+ * Vocab-sharded sampling, step 1 (one call per shard, e.g. one per GPU): the
+ * candidate list of every row of a column shard. For row r the list holds all
+ * logits of the shard >= the shard's k_use-th largest value, as
+ * (order-preserving key << 32 | global column) words, at
+ * d_cand + r*cap, with its length in d_count[r]; d_flags[r] gets MXS_ROW_NAN /
+ * MXS_ROW_OVERFLOW when the list cannot stand for the shard (then the row
+ * must be sampled from its full logits). col_offset is the shard's first
+ * global column. cap >= k_use.
+ */
+MXS_API int mxs_shard_candidates(const float* d_shard_logits, int64_t rows, int64_t shard_cols, int64_t ld,
+                         int64_t col_offset, int top_k, int cap, uint64_t* d_cand, uint32_t* d_count,
+                         uint32_t* d_flags, void* stream);
+
+/*
+ * Vocab-sharded sampling, step 2, after the shards' lists are gathered (e.g. by
+ * an NCCL all-gather) as nshards consecutive blocks of [rows x cap] words
+ * (d_cand_all) and [rows] counts and flags. Merges each row's lists, selects
+ * the top-k, and draws. Rows whose merge shows a tie, or whose shard flags are
+ * set, are not drawn: their d_row_flags entry gets MXS_ROW_EXACT and d_next -1,
+ * and the caller samples them with mxs_sample_topk_ex on the full row (the tie
+ * order depends on every logit of the row).
+ */
+MXS_API int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count_all, const uint32_t* d_flags_all,
+                     int nshards, int cap, int64_t rows, int64_t vocab, double temperature, int top_k,
+                     double top_p, double min_p, const double* d_u, int32_t* d_next, int32_t* d_topk_idx,
+                     double* d_topk_prob, uint32_t* d_row_flags, void* stream);
+
+/* OR of MXS_ROW_* flags of every row that hit MXS_ROW_TIMEOUT since the last clear
+ * on the current device (synchronises the device). */
+MXS_API int mxs_get_status(uint32_t* flags, int clear);
+
+/* Library version string. */
+MXS_API const char* mxs_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MXS_SAMPLER_H */

@@ -1,0 +1,394 @@
+// C ABI of the sampler (include/mxs_sampler.h): argument checks with the
+// reference's clamps, launch planning, workspace layout, host-buffer path.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include <cuda_runtime.h>
+
+#include "../../include/mxs_sampler.h"
+#include "mxs_launch.h"
+#include "mxs_sampler_kernel.cuh"
+
+namespace {
+
+using mxs::Params;
+
+constexpr int MAX_DEVICES = 64;
+
+struct HostBuffers {
+    float* logits = nullptr;
+    size_t logits_bytes = 0;
+    double* u = nullptr;
+    int32_t* next = nullptr;
+    int32_t* idx = nullptr;
+    double* prob = nullptr;
+    size_t rows_cap = 0, topk_cap = 0;
+};
+
+struct Device {
+    bool ready = false;
+    int sms = 0;
+    int blocks_per_sm = 0;
+    void* ws = nullptr;  // library-owned workspace (zeroed at allocation)
+    size_t ws_bytes = 0;
+    HostBuffers hb;
+};
+
+std::mutex g_mu;
+Device g_dev[MAX_DEVICES];
+
+int current_device(Device** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return MXS_ERR_NO_DEVICE;
+    Device& d = g_dev[dev];
+    if (!d.ready) {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return MXS_ERR_NO_DEVICE;
+        if (prop.major != 10) return MXS_ERR_NO_DEVICE;  // built for sm_100a only
+        int bps = 0;
+        if (mxs::sample_kernel_configure(&bps) != cudaSuccess || bps < 1) return MXS_ERR_CUDA;
+        d.sms = prop.multiProcessorCount;
+        d.blocks_per_sm = bps;
+        d.ready = true;
+    }
+    *out = &d;
+    return MXS_OK;
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Launch plan and workspace layout for one call.
+struct Plan {
+    int k_use = 1;
+    int S = 1, tpc = 1, grid = 1, outcap = 0;
+    int64_t units = 0;
+    size_t off_counter = 0, off_state = 0, off_status = 0, off_ccount = 0, off_cand = 0, off_heap = 0,
+           off_prob = 0, total = 0;
+};
+
+int clamp_k(int top_k, int64_t vocab) {
+    int64_t k = top_k <= 0 ? 1 : top_k;  // src/api/minxfmr.cpp:1567, :2091-2093
+    if (k > vocab) k = vocab;
+    return (int)k;
+}
+
+Plan make_plan(const Device& d, int64_t rows, int64_t vocab, int k_use, bool merge_mode) {
+    Plan pl;
+    pl.k_use = k_use;
+    const int64_t full = (int64_t)d.sms * d.blocks_per_sm;
+    const int64_t ntl = (vocab + mxs::TILE - 1) / mxs::TILE;
+    if (merge_mode || k_use > mxs::KFAST) {
+        pl.S = 1;
+        pl.tpc = (int)ntl;
+        pl.units = rows;
+        pl.grid = (int)std::max<int64_t>(1, std::min<int64_t>(rows, full));
+    } else {
+        int64_t s0 = std::max<int64_t>(1, full / std::max<int64_t>(rows, 1));
+        s0 = std::min(s0, ntl);
+        const int64_t tpc = (ntl + s0 - 1) / s0;
+        pl.S = (int)((ntl + tpc - 1) / tpc);
+        pl.tpc = (int)tpc;
+        pl.units = rows * pl.S;
+        pl.grid = (int)std::max<int64_t>(1, std::min<int64_t>(pl.units, full));
+    }
+    pl.outcap = pl.S > 1 ? k_use + 256 : 0;
+    size_t o = 0;
+    pl.off_status = o;
+    o = align_up(o + 256, 256);
+    // The per-row counters must read zero at the start of every call; the kernel
+    // leaves them zero. They only exist for S > 1, which needs rows < `full`, so
+    // they sit at offsets that depend on the device alone and never alias the
+    // (call-dependent) candidate lists of an earlier call.
+    pl.off_counter = o;
+    o = align_up(o + sizeof(uint32_t) * (size_t)full, 256);
+    pl.off_state = o;
+    o = align_up(o + sizeof(uint32_t) * (size_t)full, 256);
+    pl.off_ccount = o;
+    if (pl.S > 1) {
+        o = align_up(o + sizeof(uint32_t) * (size_t)rows * pl.S, 256);
+        pl.off_cand = o;
+        o = align_up(o + sizeof(uint64_t) * (size_t)rows * pl.S * pl.outcap, 256);
+    }
+    if (k_use > mxs::HEAP_SMEM_MAX && !merge_mode) {
+        pl.off_heap = o;
+        o = align_up(o + sizeof(mxs::Ent) * (size_t)pl.grid * k_use, 256);
+        pl.off_prob = o;
+        o = align_up(o + sizeof(double) * (size_t)pl.grid * k_use, 256);
+    }
+    pl.total = o;
+    return pl;
+}
+
+int ensure_library_ws(Device& d, size_t bytes, cudaStream_t stream) {
+    if (d.ws_bytes >= bytes) return MXS_OK;
+    if (d.ws) {
+        // Earlier calls on any stream may still use the old buffer.
+        if (cudaDeviceSynchronize() != cudaSuccess) return MXS_ERR_CUDA;
+        cudaFree(d.ws);
+        d.ws = nullptr;
+        d.ws_bytes = 0;
+    }
+    size_t want = std::max<size_t>(bytes, 1 << 20);
+    if (cudaMalloc(&d.ws, want) != cudaSuccess) return MXS_ERR_CUDA;
+    if (cudaMemsetAsync(d.ws, 0, want, stream) != cudaSuccess) return MXS_ERR_CUDA;
+    d.ws_bytes = want;
+    return MXS_OK;
+}
+
+void fill_workspace(Params& p, const Plan& pl, void* ws) {
+    char* b = static_cast<char*>(ws);
+    p.status = reinterpret_cast<uint32_t*>(b + pl.off_status);
+    p.row_counter = reinterpret_cast<uint32_t*>(b + pl.off_counter);
+    p.row_state = reinterpret_cast<uint32_t*>(b + pl.off_state);
+    p.chunk_count = reinterpret_cast<uint32_t*>(b + pl.off_ccount);
+    p.chunk_cand = pl.S > 1 ? reinterpret_cast<uint64_t*>(b + pl.off_cand) : nullptr;
+    p.heap_ws = pl.off_heap ? reinterpret_cast<mxs::Ent*>(b + pl.off_heap) : nullptr;
+    p.prob_ws = pl.off_prob ? reinterpret_cast<double*>(b + pl.off_prob) : nullptr;
+}
+
+void clamp_p(double* top_p, double* min_p) {  // src/api/minxfmr.cpp:2109-2111
+    if (*top_p <= 0.0 || *top_p > 1.0) *top_p = 1.0;
+    if (*min_p < 0.0) *min_p = 0.0;
+    if (*min_p > 1.0) *min_p = 1.0;
+}
+
+int launch(Params& p, const Plan& pl, cudaStream_t stream) {
+    p.S = pl.S;
+    p.tiles_per_chunk = pl.tpc;
+    p.units = pl.units;
+    p.outcap = pl.outcap;
+    const bool tma = (reinterpret_cast<uintptr_t>(p.logits) % 16 == 0) && (p.ld % 4 == 0);
+    if (mxs::sample_kernel_launch(p, pl.grid, tma, stream) != cudaSuccess) return MXS_ERR_CUDA;
+    return MXS_OK;
+}
+
+bool ws_ok(const void* ws, size_t bytes, size_t need) {
+    return ws && (reinterpret_cast<uintptr_t>(ws) % 256 == 0) && bytes >= need;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mxs_version(void) { return "mxs-sampler 0.1 sm_100a"; }
+
+int mxs_workspace_size(int64_t rows, int64_t vocab, int top_k, size_t* bytes) {
+    if (!bytes || rows < 0 || vocab <= 0 || vocab > INT32_MAX) return MXS_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Device* d;
+    int rc = current_device(&d);
+    if (rc) return rc;
+    *bytes = make_plan(*d, rows, vocab, clamp_k(top_k, vocab), false).total;
+    return MXS_OK;
+}
+
+int mxs_workspace_init(void* d_workspace, size_t workspace_bytes, void* stream) {
+    if (!d_workspace) return MXS_ERR_INVALID;
+    return cudaMemsetAsync(d_workspace, 0, workspace_bytes, (cudaStream_t)stream) == cudaSuccess ? MXS_OK
+                                                                                                : MXS_ERR_CUDA;
+}
+
+int mxs_sample_topk_ex(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
+                       int top_k, double top_p, double min_p, const double* d_u, int32_t* d_next,
+                       int32_t* d_topk_idx, double* d_topk_prob, uint32_t* d_row_flags, void* d_workspace,
+                       size_t workspace_bytes, void* stream) {
+    if (rows < 0 || vocab <= 0 || vocab > INT32_MAX || ld < vocab) return MXS_ERR_INVALID;
+    if (rows == 0) return MXS_OK;
+    if (!d_logits || !d_u || !d_next) return MXS_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Device* d;
+    int rc = current_device(&d);
+    if (rc) return rc;
+    clamp_p(&top_p, &min_p);
+    const Plan pl = make_plan(*d, rows, vocab, clamp_k(top_k, vocab), false);
+    void* ws = d_workspace;
+    if (!ws) {
+        rc = ensure_library_ws(*d, pl.total, (cudaStream_t)stream);
+        if (rc) return rc;
+        ws = d->ws;
+    } else if (!ws_ok(ws, workspace_bytes, pl.total)) {
+        return MXS_ERR_WORKSPACE;
+    }
+    Params p{};
+    p.logits = d_logits;
+    p.rows = rows;
+    p.vocab = vocab;
+    p.ld = ld;
+    p.temperature = temperature;
+    p.top_p = top_p;
+    p.min_p = min_p;
+    p.k_use = pl.k_use;
+    p.u = d_u;
+    p.next = d_next;
+    p.topk_idx = d_topk_idx;
+    p.topk_prob = d_topk_prob;
+    p.row_flags = d_row_flags;
+    p.mode = mxs::MODE_SAMPLE;
+    fill_workspace(p, pl, ws);
+    return launch(p, pl, (cudaStream_t)stream);
+}
+
+int mxs_sample_topk(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
+                    int top_k, const double* d_u, int32_t* d_next, int32_t* d_topk_idx, double* d_topk_prob,
+                    void* stream) {
+    return mxs_sample_topk_ex(d_logits, rows, vocab, ld, temperature, top_k, 1.0, 0.0, d_u, d_next, d_topk_idx,
+                              d_topk_prob, nullptr, nullptr, 0, stream);
+}
+
+int mxs_sample_topk_host(const float* h_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
+                         int top_k, double top_p, double min_p, const double* h_u, int32_t* h_next,
+                         int32_t* h_topk_idx, double* h_topk_prob, void* stream) {
+    if (rows < 0 || vocab <= 0 || vocab > INT32_MAX || ld < vocab) return MXS_ERR_INVALID;
+    if (rows == 0) return MXS_OK;
+    if (!h_logits || !h_u || !h_next) return MXS_ERR_INVALID;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int k_use = clamp_k(top_k, vocab);
+    HostBuffers* hb;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        Device* d;
+        int rc = current_device(&d);
+        if (rc) return rc;
+        hb = &d->hb;
+        const size_t lb = sizeof(float) * (size_t)rows * vocab;
+        const size_t tk = (size_t)rows * k_use;
+        if (hb->logits_bytes < lb || hb->rows_cap < (size_t)rows || hb->topk_cap < tk) {
+            if (cudaDeviceSynchronize() != cudaSuccess) return MXS_ERR_CUDA;
+            cudaFree(hb->logits);
+            cudaFree(hb->u);
+            cudaFree(hb->next);
+            cudaFree(hb->idx);
+            cudaFree(hb->prob);
+            *hb = HostBuffers{};
+            if (cudaMalloc(&hb->logits, lb) != cudaSuccess || cudaMalloc(&hb->u, sizeof(double) * rows) != cudaSuccess ||
+                cudaMalloc(&hb->next, sizeof(int32_t) * rows) != cudaSuccess ||
+                cudaMalloc(&hb->idx, sizeof(int32_t) * tk) != cudaSuccess ||
+                cudaMalloc(&hb->prob, sizeof(double) * tk) != cudaSuccess)
+                return MXS_ERR_CUDA;
+            hb->logits_bytes = lb;
+            hb->rows_cap = rows;
+            hb->topk_cap = tk;
+        }
+    }
+    // Logits are packed densely on the device (ld = vocab).
+    cudaError_t e;
+    if (ld == vocab)
+        e = cudaMemcpyAsync(hb->logits, h_logits, sizeof(float) * rows * vocab, cudaMemcpyHostToDevice, st);
+    else
+        e = cudaMemcpy2DAsync(hb->logits, sizeof(float) * vocab, h_logits, sizeof(float) * ld, sizeof(float) * vocab,
+                              rows, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return MXS_ERR_CUDA;
+    if (cudaMemcpyAsync(hb->u, h_u, sizeof(double) * rows, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return MXS_ERR_CUDA;
+    int rc = mxs_sample_topk_ex(hb->logits, rows, vocab, vocab, temperature, top_k, top_p, min_p, hb->u, hb->next,
+                                h_topk_idx ? hb->idx : nullptr, h_topk_prob ? hb->prob : nullptr, nullptr, nullptr, 0,
+                                stream);
+    if (rc) return rc;
+    if (cudaMemcpyAsync(h_next, hb->next, sizeof(int32_t) * rows, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return MXS_ERR_CUDA;
+    if (h_topk_idx && cudaMemcpyAsync(h_topk_idx, hb->idx, sizeof(int32_t) * rows * k_use, cudaMemcpyDeviceToHost,
+                                      st) != cudaSuccess)
+        return MXS_ERR_CUDA;
+    if (h_topk_prob && cudaMemcpyAsync(h_topk_prob, hb->prob, sizeof(double) * rows * k_use,
+                                       cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return MXS_ERR_CUDA;
+    return cudaStreamSynchronize(st) == cudaSuccess ? MXS_OK : MXS_ERR_CUDA;
+}
+
+int mxs_shard_candidates(const float* d_shard_logits, int64_t rows, int64_t shard_cols, int64_t ld,
+                         int64_t col_offset, int top_k, int cap, uint64_t* d_cand, uint32_t* d_count,
+                         uint32_t* d_flags, void* stream) {
+    if (rows < 0 || shard_cols <= 0 || ld < shard_cols || col_offset < 0 || col_offset + shard_cols > INT32_MAX)
+        return MXS_ERR_INVALID;
+    if (rows == 0) return MXS_OK;
+    if (!d_shard_logits || !d_cand || !d_count || !d_flags) return MXS_ERR_INVALID;
+    const int k_use = clamp_k(top_k, shard_cols);
+    if (cap < k_use) return MXS_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Device* d;
+    int rc = current_device(&d);
+    if (rc) return rc;
+    const Plan pl = make_plan(*d, rows, shard_cols, k_use, false);
+    rc = ensure_library_ws(*d, pl.total, (cudaStream_t)stream);
+    if (rc) return rc;
+    Params p{};
+    p.logits = d_shard_logits;
+    p.rows = rows;
+    p.vocab = shard_cols;
+    p.ld = ld;
+    p.k_use = k_use;
+    p.mode = mxs::MODE_EMIT;
+    p.col_offset = col_offset;
+    p.out_cand = d_cand;
+    p.out_count = d_count;
+    p.out_flags = d_flags;
+    p.out_cap = cap;
+    fill_workspace(p, pl, d->ws);
+    return launch(p, pl, (cudaStream_t)stream);
+}
+
+int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count_all, const uint32_t* d_flags_all,
+                     int nshards, int cap, int64_t rows, int64_t vocab, double temperature, int top_k, double top_p,
+                     double min_p, const double* d_u, int32_t* d_next, int32_t* d_topk_idx, double* d_topk_prob,
+                     uint32_t* d_row_flags, void* stream) {
+    if (rows < 0 || vocab <= 0 || vocab > INT32_MAX || nshards <= 0 || cap <= 0) return MXS_ERR_INVALID;
+    if (rows == 0) return MXS_OK;
+    if (!d_cand_all || !d_count_all || !d_u || !d_next) return MXS_ERR_INVALID;
+    const int k_use = clamp_k(top_k, vocab);
+    if (k_use > mxs::KFAST) return MXS_ERR_INVALID;  // the merge keeps at most KFAST survivors
+    std::lock_guard<std::mutex> lk(g_mu);
+    Device* d;
+    int rc = current_device(&d);
+    if (rc) return rc;
+    clamp_p(&top_p, &min_p);
+    const Plan pl = make_plan(*d, rows, vocab, k_use, true);
+    rc = ensure_library_ws(*d, pl.total, (cudaStream_t)stream);
+    if (rc) return rc;
+    Params p{};
+    p.rows = rows;
+    p.vocab = vocab;
+    p.ld = vocab;
+    p.temperature = temperature;
+    p.top_p = top_p;
+    p.min_p = min_p;
+    p.k_use = k_use;
+    p.u = d_u;
+    p.next = d_next;
+    p.topk_idx = d_topk_idx;
+    p.topk_prob = d_topk_prob;
+    p.row_flags = d_row_flags;
+    p.mode = mxs::MODE_MERGE;
+    p.in_cand = d_cand_all;
+    p.in_count = d_count_all;
+    p.in_flags = d_flags_all;
+    p.nshards = nshards;
+    p.in_cap = cap;
+    fill_workspace(p, pl, d->ws);
+    p.logits = nullptr;
+    // no logits: launch the plain variant (no bulk copies are issued in merge mode)
+    p.S = pl.S;
+    p.tiles_per_chunk = pl.tpc;
+    p.units = pl.units;
+    p.outcap = 0;
+    if (mxs::sample_kernel_launch(p, pl.grid, false, (cudaStream_t)stream) != cudaSuccess) return MXS_ERR_CUDA;
+    return MXS_OK;
+}
+
+int mxs_get_status(uint32_t* flags, int clear) {
+    if (!flags) return MXS_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Device* d;
+    int rc = current_device(&d);
+    if (rc) return rc;
+    *flags = 0;
+    if (!d->ws) return MXS_OK;
+    if (cudaDeviceSynchronize() != cudaSuccess) return MXS_ERR_CUDA;
+    // status sits at offset 0 of every workspace layout
+    if (cudaMemcpy(flags, d->ws, sizeof(uint32_t), cudaMemcpyDeviceToHost) != cudaSuccess) return MXS_ERR_CUDA;
+    if (clear && cudaMemset(d->ws, 0, sizeof(uint32_t)) != cudaSuccess) return MXS_ERR_CUDA;
+    return MXS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,180 @@
+// Row finishing for the fused sampler: the draw (softmax over the k survivors,
+// then the inverse-CDF pick) and the exact heap replay for rows with ties.
+#pragma once
+
+#include "mxs_sampler_kernel.cuh"
+
+namespace mxs {
+
+// First i in cp[0, n) with !(cp[i] < u): std::lower_bound's bisection, step for
+// step, so NaNs in cp land where the reference's lower_bound lands.
+__device__ __forceinline__ int lower_bound_cp(const double* cp, int n, double u) {
+    int first = 0, len = n;
+    while (len > 0) {
+        const int half = len >> 1;
+        if (cp[first + half] < u) {
+            first += half + 1;
+            len -= half + 1;
+        } else {
+            len = half;
+        }
+    }
+    return first;
+}
+
+// e[0, k): the row's top-k in the reference's order. pbuf: k doubles.
+// Follows src/api/minxfmr.cpp:2104-2169 and libstdc++'s discrete_distribution
+// (bits/random.tcc:2657-2714): each double operation of the reference happens
+// here in the same order on the same operands. The k exps and the divisions are
+// independent and run across the CTA; the three running sums stay sequential.
+__device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, int k, double* pbuf, Misc& sm) {
+    const int tid = threadIdx.x;
+    if (p.topk_idx)
+        for (int i = tid; i < k; i += NT) p.topk_idx[row * k + i] = e[i].i;
+    const double T = p.temperature;
+    bool greedy = (T <= 0.0);
+    double sum = 0.0;
+    if (!greedy) {
+        const double maxs = (double)e[0].v;
+        for (int i = tid; i < k; i += NT) pbuf[i] = exp(((double)e[i].v - maxs) / T);
+        __syncthreads();
+        if (tid == 0) {
+            double s = 0.0;
+            for (int i = 0; i < k; ++i) s += pbuf[i];
+            sm.sum = s;
+        }
+        __syncthreads();
+        sum = sm.sum;
+        greedy = (sum <= 0.0);
+    }
+    if (greedy) {
+        if (p.topk_prob)
+            for (int i = tid; i < k; i += NT) p.topk_prob[row * k + i] = (i == 0) ? 1.0 : 0.0;
+        if (tid == 0) p.next[row] = e[0].i;
+        __syncthreads();
+        return;
+    }
+    for (int i = tid; i < k; i += NT) {
+        const double q = pbuf[i] / sum;
+        pbuf[i] = q;
+        if (p.topk_prob) p.topk_prob[row * k + i] = q;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int n = k;
+        if (p.top_p < 1.0) {  // src/api/minxfmr.cpp:2128-2145
+            double cum = 0.0;
+            n = 0;
+            for (int i = 0; i < k; ++i) {
+                cum += pbuf[i];
+                n = i + 1;
+                if (cum >= p.top_p) break;
+            }
+            if (n < 1) n = 1;
+            double renorm = 0.0;
+            for (int i = 0; i < n; ++i) renorm += pbuf[i];
+            if (renorm > 0.0)
+                for (int i = 0; i < n; ++i) pbuf[i] /= renorm;
+        }
+        if (p.min_p > 0.0 && n > 1) {  // src/api/minxfmr.cpp:2147-2165
+            const double thr = pbuf[0] * p.min_p;
+            int keep = 1;
+            for (int i = 1; i < n; ++i) {
+                if (pbuf[i] >= thr) keep = i + 1;
+                else break;
+            }
+            n = keep;
+            double renorm = 0.0;
+            for (int i = 0; i < n; ++i) renorm += pbuf[i];
+            if (renorm > 0.0)
+                for (int i = 0; i < n; ++i) pbuf[i] /= renorm;
+        }
+        sm.krem = n;
+        double s2 = 0.0;
+        if (n >= 2)
+            for (int i = 0; i < n; ++i) s2 += pbuf[i];
+        sm.sum = s2;
+    }
+    __syncthreads();
+    const int n = sm.krem;
+    if (n < 2) {  // discrete_distribution with fewer than two weights returns 0
+        if (tid == 0) p.next[row] = e[0].i;
+        __syncthreads();
+        return;
+    }
+    const double s2 = sm.sum;
+    for (int i = tid; i < n; i += NT) pbuf[i] = pbuf[i] / s2;
+    __syncthreads();
+    if (tid == 0) {
+        double run = 0.0;
+        for (int i = 0; i < n; ++i) {
+            run += pbuf[i];
+            pbuf[i] = run;
+        }
+        pbuf[n - 1] = 1.0;
+        p.next[row] = e[lower_bound_cp(pbuf, n, p.u[row])].i;
+    }
+    __syncthreads();
+}
+
+// Exact replay of the reference's partial_sort heap process over row `row`,
+// then the draw. `nan_state`: 1 = the row holds a NaN, 0 = it holds none,
+// -1 = unknown (scanned here). With a NaN anywhere the heap order is no longer
+// a total order, the root can shrink, and the lower-bound filter is not valid:
+// every element is then offered serially.
+__device__ inline void exact_row(const Params& p, int64_t row, int nan_state, unsigned char* region, Misc& sm) {
+    const int tid = threadIdx.x;
+    const int k = p.k_use;
+    const int64_t V = p.vocab;
+    const float* x = p.logits + row * p.ld;
+    const bool small = (k <= HEAP_SMEM_MAX);
+    Ent* h = small ? reinterpret_cast<Ent*>(region) : p.heap_ws + (int64_t)blockIdx.x * k;
+    Ent* xl = reinterpret_cast<Ent*>(region + HEAP_SMEM_MAX * sizeof(Ent));
+    double* pbuf = small ? reinterpret_cast<double*>(region + HEAP_SMEM_MAX * sizeof(Ent))
+                         : p.prob_ws + (int64_t)blockIdx.x * k;
+
+    if (nan_state < 0) {
+        int has = 0;
+        for (int64_t j = tid; j < V; j += NT) has |= (x[j] != x[j]);
+        nan_state = __syncthreads_or(has) ? 1 : 0;
+    }
+    for (int i = tid; i < k; i += NT) h[i] = Ent{x[i], i};
+    __syncthreads();
+    if (tid == 0) heap_build(h, k);
+    __syncthreads();
+    if (k < V) {
+        if (nan_state) {
+            if (tid == 0)
+                for (int64_t j = k; j < V; ++j) heap_offer(h, k, Ent{x[j], (int32_t)j});
+            __syncthreads();
+        } else {
+            constexpr int PER = XTILE / NT;
+            for (int64_t base = k; base < V; base += XTILE) {
+                const float r0 = h[0].v;
+                float xv[PER];
+                int c = 0;
+#pragma unroll
+                for (int q = 0; q < PER; ++q) {
+                    const int64_t j = base + (int64_t)tid * PER + q;
+                    xv[q] = (j < V) ? x[j] : r0;
+                    c += (xv[q] > r0) ? 1 : 0;
+                }
+                int total;
+                int pos = block_excl_scan(c, sm, &total);
+#pragma unroll
+                for (int q = 0; q < PER; ++q) {
+                    if (xv[q] > r0) xl[pos++] = Ent{xv[q], (int32_t)(base + (int64_t)tid * PER + q)};
+                }
+                __syncthreads();
+                if (tid == 0)
+                    for (int i = 0; i < total; ++i) heap_offer(h, k, xl[i]);
+                __syncthreads();
+            }
+        }
+    }
+    if (tid == 0) heap_sort(h, k);
+    __syncthreads();
+    block_draw(p, row, h, k, pbuf, sm);
+}
+
+}  // namespace mxs

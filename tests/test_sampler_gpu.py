@@ -1,0 +1,174 @@
+"""GPU parity of the CUDA sampler (through the C ABI) against the CPU oracle and
+the golden fixtures made by the reference's own sampling block.
+
+Bar: next ids, top-k index set and tie order bit-exact; probabilities within
+1e-6 relative (fp64 arithmetic in the same order; CUDA's exp and glibc's may
+differ by an ulp)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle_lib
+import workloads
+from test_oracle import GOLDEN_CASES, check_against_golden, golden_logits
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-6
+
+
+def run_gpu(mxs, x, T, k, u, top_p=1.0, min_p=0.0, ld=None, offset=0, workspace=None):
+    rows, V = x.shape
+    if ld is None and offset == 0:
+        lg = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    else:
+        ld = ld or V
+        buf = torch.full((rows * ld + offset + 8,), float("nan"), dtype=torch.float32)
+        view = buf[offset:offset + rows * ld].view(rows, ld)
+        view[:, :V] = torch.from_numpy(x)
+        lg = buf.cuda()[offset:offset + rows * ld].view(rows, ld)[:, :V]
+    uu = torch.from_numpy(np.ascontiguousarray(u, dtype=np.float64)).cuda()
+    nxt, idx, prob, flags = mxs.sample(lg, T, k, uu, top_p, min_p, return_flags=True, workspace=workspace)
+    torch.cuda.synchronize()
+    return nxt.cpu().numpy(), idx.cpu().numpy(), prob.cpu().numpy(), flags.cpu().numpy()
+
+
+def assert_parity(x, T, k, u, got, top_p=1.0, min_p=0.0, name=""):
+    n0, i0, p0 = oracle_lib.oracle_sample(x, T, k, u, top_p, min_p)
+    nxt, idx, prob = got[:3]
+    bad = np.nonzero(nxt != n0)[0]
+    assert bad.size == 0, f"{name}: next differs on rows {bad[:10]} ({bad.size} rows)"
+    bad = np.nonzero((idx != i0).any(axis=1))[0]
+    assert bad.size == 0, f"{name}: top-k order differs on rows {bad[:10]}"
+    np.testing.assert_allclose(prob, p0, rtol=RTOL, atol=0, err_msg=name)
+
+
+@pytest.mark.parametrize("c", GOLDEN_CASES, ids=[c["name"] for c in GOLDEN_CASES])
+def test_gpu_matches_reference_golden(mxs, c):
+    x = golden_logits(c)
+    u = oracle_lib.uniforms(c["seed"], x.shape[0])
+    nxt, idx, prob, _ = run_gpu(mxs, x, c["T"], c["k"], u, c["top_p"], c["min_p"])
+    check_against_golden(c, nxt, idx, prob)
+
+
+@pytest.mark.parametrize("name", ["c1_single_row", "c2_batched_spiked", "c4_ties_k1024"])
+def test_config_full_size(mxs, name):
+    gen, T, k = workloads.CONFIGS[name]
+    x = gen(100)
+    u = oracle_lib.uniforms(100, x.shape[0])
+    got = run_gpu(mxs, x, T, k, u)
+    assert_parity(x, T, k, u, got, name=name)
+    if name == "c4_ties_k1024":
+        assert (got[3] & mxs.ROW_EXACT).all(), "quantised Gumbel rows must take the exact replay"
+
+
+@pytest.mark.parametrize("k", workloads.C3_KS)
+def test_config3_edge_sweep(mxs, k):
+    x = workloads.c3_edge(101, rows=512 if k != workloads.V_LLAMA3 else 64)
+    for T in workloads.C3_TS:
+        u = oracle_lib.uniforms(101 + int(T * 10), x.shape[0])
+        got = run_gpu(mxs, x, T, k, u)
+        assert_parity(x, T, k, u, got, name=f"c3 k={k} T={T}")
+
+
+@pytest.mark.parametrize("rows", [1, 16, 256, 1024, 4096])
+def test_config5_throughput_shapes(mxs, rows):
+    x = workloads.normal(105 + rows, rows, workloads.V_QWEN, 2.0)
+    u = oracle_lib.uniforms(105, rows)
+    got = run_gpu(mxs, x, 0.8, 50, u)
+    assert_parity(x, 0.8, 50, u, got, name=f"c5 rows={rows}")
+
+
+def test_ragged_vocab_strided_and_unaligned(mxs):
+    rng = np.random.default_rng(11)
+    for V, ld, off in [(1, 1, 0), (2, 3, 0), (3, 3, 1), (7, 9, 2), (4097, 4101, 1), (10001, 10001, 3),
+                       (151936, 152000, 0), (151935, 151935, 0), (4096 * 3 + 1, 4096 * 3 + 4, 0)]:
+        x = rng.standard_normal((5, V)).astype(np.float32)
+        u = rng.random(5)
+        for k in (1, 3, 50):
+            got = run_gpu(mxs, x, 0.9, k, u, ld=ld, offset=off)
+            assert_parity(x, 0.9, k, u, got, name=f"V={V} ld={ld} off={off} k={k}")
+
+
+def test_special_values_and_degenerate_rows(mxs):
+    V = 20000
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((8, V)).astype(np.float32)
+    x[0, :] = 0.0                       # all equal: overflow of the candidate buffer -> exact path
+    x[1, :] = -np.inf                   # all -inf: NaN probabilities, as the reference
+    x[2, 123] = np.nan                  # a NaN
+    x[3, ::2] = -0.0                    # signed zeros mixed with values
+    x[3, 1::2] = 0.0
+    x[4, 77] = np.inf                   # +inf dominates
+    x[5, :100] = 5.0                    # ties at the top, inside the first k
+    x[6, rng.random(V) < 0.5] = -np.inf
+    x[7, 5000:5100] = 3.0
+    u = rng.random(8)
+    for k in (1, 2, 64, 300):
+        for T in (0.0, 0.5, 1.5):
+            got = run_gpu(mxs, x, T, k, u)
+            assert_parity(x, T, k, u, got, name=f"special k={k} T={T}")
+
+
+def test_top_p_min_p_and_clamps(mxs):
+    x = workloads.spiked(13, 32, 50000)
+    u = oracle_lib.uniforms(13, 32)
+    for k in (0, 1, 40, 60000):
+        for top_p, min_p in [(0.9, 0.0), (0.5, 0.05), (1.0, 0.2), (0.0, -1.0), (2.0, 3.0)]:
+            got = run_gpu(mxs, x, 0.7, k, u, top_p, min_p)
+            n0, i0, p0 = oracle_lib.oracle_sample(x, 0.7, k, u, top_p, min_p)
+            np.testing.assert_array_equal(got[0], n0)
+            np.testing.assert_array_equal(got[1], i0)
+
+
+def test_large_k_global_heap(mxs):
+    x = workloads.normal(14, 8, 40000, 1.0)
+    x = np.round(x * 64) / 64
+    u = oracle_lib.uniforms(14, 8)
+    for k in (2049, 5000, 40000):
+        got = run_gpu(mxs, x.astype(np.float32), 1.0, k, u)
+        assert_parity(x.astype(np.float32), 1.0, k, u, got, name=f"large k={k}")
+
+
+def test_caller_workspace_and_repeat_calls(mxs):
+    x = workloads.normal(15, 3, workloads.V_QWEN, 2.0)
+    u = oracle_lib.uniforms(15, 3)
+    ws = mxs.make_workspace(3, workloads.V_QWEN, 50)
+    for _ in range(3):
+        got = run_gpu(mxs, x, 0.8, 50, u, workspace=ws)
+        assert_parity(x, 0.8, 50, u, got, name="caller workspace")
+    with pytest.raises(mxs.SamplerError):
+        small = torch.zeros(16, dtype=torch.uint8, device="cuda")
+        run_gpu(mxs, x, 0.8, 50, u, workspace=small)
+
+
+def test_host_entry_point(mxs):
+    x = workloads.spiked(16, 64, workloads.V_QWEN)
+    u = oracle_lib.uniforms(16, 64)
+    nxt, idx, prob = mxs.sample_host(x, 0.7, 40, u, return_topk=True)
+    assert_parity(x, 0.7, 40, u, (nxt, idx, prob), name="host entry")
+
+
+def test_vocab_sharded_merge_on_one_gpu(mxs):
+    """8 column shards sampled separately and merged equal the unsharded call."""
+    rows, V, k, T = 64, workloads.V_QWEN, 50, 0.8
+    x = workloads.normal(17, rows, V, 2.0)
+    x[3, 1000:1040] = 7.5  # a tie row: handed back by the merge
+    u = oracle_lib.uniforms(17, rows)
+    lg = torch.from_numpy(x).cuda()
+    uu = torch.from_numpy(u).cuda()
+    cols = V // 8
+    cap = 2 * k
+    parts = [mxs.shard_candidates(lg[:, s * cols:(s + 1) * cols], s * cols, k, cap) for s in range(8)]
+    cand = torch.stack([p[0] for p in parts])
+    cnt = torch.stack([p[1] for p in parts])
+    flg = torch.stack([p[2] for p in parts])
+    nxt, idx, prob, rflg = mxs.merge_sample(cand, cnt, flg, V, T, k, uu)
+    torch.cuda.synchronize()
+    nxt, idx, prob, rflg = (t.cpu().numpy() for t in (nxt, idx, prob, rflg))
+    n0, i0, p0 = oracle_lib.oracle_sample(x, T, k, u)
+    exact = (rflg & mxs.ROW_EXACT) != 0
+    assert exact[3] and nxt[3] == -1
+    np.testing.assert_array_equal(nxt[~exact], n0[~exact])
+    np.testing.assert_array_equal(idx[~exact], i0[~exact])
+    np.testing.assert_allclose(prob[~exact], p0[~exact], rtol=RTOL, atol=0)
