@@ -2,6 +2,7 @@
 // reference's clamps, launch planning, workspace layout, host-buffer path.
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -160,6 +161,10 @@ int launch(Params& p, const Plan& pl, cudaStream_t stream) {
     p.units = pl.units;
     p.outcap = pl.outcap;
     const bool tma = (reinterpret_cast<uintptr_t>(p.logits) % 16 == 0) && (p.ld % 4 == 0);
+    // MXS_SAMPLER_BLOCK_PATH=1 selects the CTA-synchronous streaming kernel for
+    // every k (the parity tests run both kernels).
+    const char* bp = getenv("MXS_SAMPLER_BLOCK_PATH");
+    p.force_block_path = (bp && bp[0] == '1') ? 1 : 0;
     if (mxs::sample_kernel_launch(p, pl.grid, tma, stream) != cudaSuccess) return MXS_ERR_CUDA;
     return MXS_OK;
 }

@@ -106,6 +106,33 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
+// Phase timers of the profiling build (-DMXS_PROFILE): thread 0 of each CTA
+// accumulates clock64 deltas per phase into g_mxs_prof[blockIdx.x][phase].
+#ifdef MXS_PROFILE
+constexpr int PROF_CTAS = 1024, PROF_PHASES = 8;
+__device__ unsigned long long g_mxs_prof[PROF_CTAS][PROF_PHASES];
+#define MXS_PROF_T0(v) long long v = (threadIdx.x == 0) ? clock64() : 0
+#define MXS_PROF_ADD(ph, v)                                                             \
+    do {                                                                                \
+        if (threadIdx.x == 0 && blockIdx.x < mxs::PROF_CTAS)                            \
+            mxs::g_mxs_prof[blockIdx.x][ph] += (unsigned long long)(clock64() - (v));   \
+    } while (0)
+#else
+#define MXS_PROF_T0(v) (void)0
+#define MXS_PROF_ADD(ph, v) (void)0
+#endif
+
+// Barrier over the CTA's NT sampling threads only (named barrier 1). A
+// warp-specialised CTA adds a producer warp that never joins it.
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
+__device__ __forceinline__ int csync_or(int pred) {
+    int r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.s32 %0, 1, 0, q;\n}"
+        : "=r"(r) : "r"(pred), "n"(NT) : "memory");
+    return r;
+}
+
 // Warp-inclusive prefix sum.
 __device__ __forceinline__ int warp_incl_scan(int v) {
     const int lane = threadIdx.x & 31;

@@ -37,13 +37,13 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
     if (!greedy) {
         const double maxs = (double)e[0].v;
         for (int i = tid; i < k; i += NT) pbuf[i] = exp(((double)e[i].v - maxs) / T);
-        __syncthreads();
+        csync();
         if (tid == 0) {
             double s = 0.0;
             for (int i = 0; i < k; ++i) s += pbuf[i];
             sm.sum = s;
         }
-        __syncthreads();
+        csync();
         sum = sm.sum;
         greedy = (sum <= 0.0);
     }
@@ -51,7 +51,7 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
         if (p.topk_prob)
             for (int i = tid; i < k; i += NT) p.topk_prob[row * k + i] = (i == 0) ? 1.0 : 0.0;
         if (tid == 0) p.next[row] = e[0].i;
-        __syncthreads();
+        csync();
         return;
     }
     for (int i = tid; i < k; i += NT) {
@@ -59,7 +59,7 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
         pbuf[i] = q;
         if (p.topk_prob) p.topk_prob[row * k + i] = q;
     }
-    __syncthreads();
+    csync();
     if (tid == 0) {
         int n = k;
         if (p.top_p < 1.0) {  // src/api/minxfmr.cpp:2128-2145
@@ -95,16 +95,16 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
             for (int i = 0; i < n; ++i) s2 += pbuf[i];
         sm.sum = s2;
     }
-    __syncthreads();
+    csync();
     const int n = sm.krem;
     if (n < 2) {  // discrete_distribution with fewer than two weights returns 0
         if (tid == 0) p.next[row] = e[0].i;
-        __syncthreads();
+        csync();
         return;
     }
     const double s2 = sm.sum;
     for (int i = tid; i < n; i += NT) pbuf[i] = pbuf[i] / s2;
-    __syncthreads();
+    csync();
     if (tid == 0) {
         double run = 0.0;
         for (int i = 0; i < n; ++i) {
@@ -114,7 +114,7 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
         pbuf[n - 1] = 1.0;
         p.next[row] = e[lower_bound_cp(pbuf, n, p.u[row])].i;
     }
-    __syncthreads();
+    csync();
 }
 
 // Exact replay of the reference's partial_sort heap process over row `row`,
@@ -136,17 +136,17 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
     if (nan_state < 0) {
         int has = 0;
         for (int64_t j = tid; j < V; j += NT) has |= (x[j] != x[j]);
-        nan_state = __syncthreads_or(has) ? 1 : 0;
+        nan_state = csync_or(has) ? 1 : 0;
     }
     for (int i = tid; i < k; i += NT) h[i] = Ent{x[i], i};
-    __syncthreads();
+    csync();
     if (tid == 0) heap_build(h, k);
-    __syncthreads();
+    csync();
     if (k < V) {
         if (nan_state) {
             if (tid == 0)
                 for (int64_t j = k; j < V; ++j) heap_offer(h, k, Ent{x[j], (int32_t)j});
-            __syncthreads();
+            csync();
         } else {
             constexpr int PER = XTILE / NT;
             for (int64_t base = k; base < V; base += XTILE) {
@@ -165,15 +165,15 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
                 for (int q = 0; q < PER; ++q) {
                     if (xv[q] > r0) xl[pos++] = Ent{xv[q], (int32_t)(base + (int64_t)tid * PER + q)};
                 }
-                __syncthreads();
+                csync();
                 if (tid == 0)
                     for (int i = 0; i < total; ++i) heap_offer(h, k, xl[i]);
-                __syncthreads();
+                csync();
             }
         }
     }
     if (tid == 0) heap_sort(h, k);
-    __syncthreads();
+    csync();
     block_draw(p, row, h, k, pbuf, sm);
 }
 

@@ -23,7 +23,7 @@ __device__ __forceinline__ void shrink_candidates(uint32_t* ckey, int32_t* cidx,
             sm.thr = fkey_inv(kth);
         }
     }
-    __syncthreads();
+    csync();
 }
 
 // Finish row `row` from the candidate buffer (every logit >= the row's k-th
@@ -36,14 +36,52 @@ __device__ void finish_row(const Params& p, int64_t row, uint32_t flags, unsigne
     bool exact = (flags & (FLAG_NAN | FLAG_OVERFLOW | FLAG_UNSCANNED)) != 0;
     if (!(flags & FLAG_TIMEOUT) && !exact) {
         int cnt = sm.cnt;
+        const bool small = (k <= 64);
         if (cnt < k) {
             exact = true;
-        } else if (cnt > k) {
+        } else if (cnt > k && !(small && cnt <= 64)) {
             const uint32_t kth = block_select_kth(ckey, cnt, k, sm);
             cnt = block_compact_ge(ckey, cidx, sm, cnt, kth);
             exact = (cnt != k);  // more than k at or above the cut: a tie straddles it
         }
-        if (!exact) {
+        MXS_PROF_T0(tsort);
+        if (!exact && small) {
+            // cnt <= 64 entries, every logit >= the k-th largest among them:
+            // one warp sorts them in registers and looks for equal neighbours
+            // among the first k (and across the cut when cnt > k).
+            if (tid < 32) {
+                const int lane = tid;
+                const uint64_t a0 = lane < cnt ? ((uint64_t)ckey[lane] << 32) | (uint32_t)cidx[lane] : 0ull;
+                const uint64_t a1 =
+                    lane + 32 < cnt ? ((uint64_t)ckey[lane + 32] << 32) | (uint32_t)cidx[lane + 32] : 0ull;
+                uint64_t b0 = a0, b1 = a1;
+                warp_sort64_desc(b0, b1);
+                const uint64_t first1 = __shfl_sync(0xffffffffu, b1, 0);
+                const uint64_t dn0 = __shfl_down_sync(0xffffffffu, b0, 1);
+                const uint64_t n1 = __shfl_down_sync(0xffffffffu, b1, 1);
+                const uint64_t n0 = (lane == 31) ? first1 : dn0;
+                const int lim = (cnt > k) ? k : k - 1;  // compare pairs (i, i+1) for i < lim
+                const bool tie = (lane < lim && (b0 >> 32) == (n0 >> 32)) ||
+                                 (lane + 32 < lim && (b1 >> 32) == (n1 >> 32));
+                const bool any = __any_sync(0xffffffffu, tie);
+                if (!any) {
+                    Ent* e = reinterpret_cast<Ent*>(region);
+                    __syncwarp();
+                    if (lane < k) e[lane] = Ent{fkey_inv((uint32_t)(b0 >> 32)), (int32_t)(uint32_t)b0};
+                    if (lane + 32 < k) e[lane + 32] = Ent{fkey_inv((uint32_t)(b1 >> 32)), (int32_t)(uint32_t)b1};
+                }
+                if (lane == 0) sm.xn = any ? 1 : 0;
+            }
+            csync();
+            exact = sm.xn != 0;
+            MXS_PROF_ADD(4, tsort);
+            if (!exact) {
+                MXS_PROF_T0(tdraw);
+                block_draw(p, row, reinterpret_cast<Ent*>(region), k, reinterpret_cast<double*>(region + SORTMAX * 8),
+                           sm);
+                MXS_PROF_ADD(5, tdraw);
+            }
+        } else if (!exact) {
             constexpr int PER = SORTMAX / NT;
             uint32_t kk[PER];
             int32_t ii[PER];
@@ -53,7 +91,7 @@ __device__ void finish_row(const Params& p, int64_t row, uint32_t flags, unsigne
                 kk[r] = (i < k) ? ckey[i] : 0u;
                 ii[r] = (i < k) ? cidx[i] : 0;
             }
-            __syncthreads();
+            csync();
             int P = 1;
             while (P < k) P <<= 1;
             uint64_t* sb = reinterpret_cast<uint64_t*>(region);
@@ -62,32 +100,39 @@ __device__ void finish_row(const Params& p, int64_t row, uint32_t flags, unsigne
                 const int i = tid + r * NT;
                 if (i < P) sb[i] = (i < k) ? ((uint64_t)kk[r] << 32) | (uint32_t)ii[r] : 0ull;
             }
-            __syncthreads();
+            csync();
             block_sort_desc(sb, P);
             int tie = 0;
             for (int i = tid; i + 1 < k; i += NT) tie |= ((sb[i] >> 32) == (sb[i + 1] >> 32));
-            exact = __syncthreads_or(tie) != 0;
+            exact = csync_or(tie) != 0;
+            MXS_PROF_ADD(4, tsort);
             if (!exact) {
+                MXS_PROF_T0(tdraw);
                 Ent* e = reinterpret_cast<Ent*>(region);
                 for (int i = tid; i < k; i += NT) {
                     const uint64_t w = sb[i];
                     e[i] = Ent{fkey_inv((uint32_t)(w >> 32)), (int32_t)(uint32_t)w};
                 }
-                __syncthreads();
+                csync();
                 block_draw(p, row, e, k, reinterpret_cast<double*>(region + SORTMAX * 8), sm);
+                MXS_PROF_ADD(5, tdraw);
             }
         }
     }
     // MODE_MERGE holds no logits: a row that needs the replay is handed back.
     const bool can_replay = (p.mode != MODE_MERGE);
-    if (!(flags & FLAG_TIMEOUT) && exact && can_replay) exact_row(p, row, (flags & FLAG_NAN) ? 1 : ((flags & FLAG_UNSCANNED) ? -1 : 0), region, sm);
+    if (!(flags & FLAG_TIMEOUT) && exact && can_replay) {
+        MXS_PROF_T0(tex);
+        exact_row(p, row, (flags & FLAG_NAN) ? 1 : ((flags & FLAG_UNSCANNED) ? -1 : 0), region, sm);
+        MXS_PROF_ADD(6, tex);
+    }
     if (tid == 0) {
         const uint32_t f = (flags & ~FLAG_UNSCANNED) | (exact ? FLAG_EXACT : 0u);
         if (p.row_flags) p.row_flags[row] = f;
         if ((f & FLAG_TIMEOUT) || (exact && !can_replay)) p.next[row] = -1;
         if (f & FLAG_TIMEOUT) atomicOr(p.status, f);
     }
-    __syncthreads();
+    csync();
 }
 
 // MODE_EMIT: publish the row's candidate list (all logits of the shard >= the
@@ -111,7 +156,7 @@ __device__ void emit_list(const Params& p, int64_t row, uint32_t flags, unsigned
         p.out_flags[row] = flags;
         if (flags & FLAG_TIMEOUT) atomicOr(p.status, flags);
     }
-    __syncthreads();
+    csync();
 }
 
 __device__ __forceinline__ void row_done(const Params& p, int64_t row, uint32_t flags, unsigned char* region,
@@ -145,10 +190,62 @@ __device__ void append_list(const uint64_t* src, int n, uint32_t* ckey, int32_t*
             }
         }
         block_append4(ckey, cidx, sm, m, key, idx);
-        __syncthreads();
+        csync();
         const int cn = sm.cnt;
         if (cn > CAP - SUB) shrink_candidates(ckey, cidx, sm, cn, k);
     }
+}
+
+// End of a (row, chunk) unit; the candidate buffer holds ckey/cidx[0, sm.cnt).
+// S == 1: finish the row. S > 1: publish this chunk's candidates >= its k-th
+// largest key; the last chunk of the row to finish merges all of them and
+// finishes the row.
+__device__ void unit_end(const Params& p, int64_t row, int c, uint32_t flags, unsigned char* region, Misc& sm) {
+    const int tid = threadIdx.x;
+    const int k = p.k_use;
+    const int S = p.S;
+    uint32_t* ckey = reinterpret_cast<uint32_t*>(region);
+    int32_t* cidx = reinterpret_cast<int32_t*>(region + CAP * 4);
+    if (S == 1) {
+        row_done(p, row, flags, region, sm);
+        return;
+    }
+    int cnt = sm.cnt;
+    if (!(flags & (FLAG_NAN | FLAG_OVERFLOW | FLAG_TIMEOUT)) && cnt > k) {
+        const uint32_t kth = block_select_kth(ckey, cnt, k, sm);
+        cnt = block_compact_ge(ckey, cidx, sm, cnt, kth);
+    }
+    if (cnt > p.outcap) flags |= FLAG_OVERFLOW;
+    const int64_t slot = row * S + c;
+    if (!(flags & FLAG_OVERFLOW)) {
+        uint64_t* dst = p.chunk_cand + slot * p.outcap;
+        for (int i = tid; i < cnt; i += NT) dst[i] = ((uint64_t)ckey[i] << 32) | (uint32_t)cidx[i];
+    }
+    if (tid == 0) {
+        p.chunk_count[slot] = (uint32_t)cnt;
+        if (flags) atomicOr(&p.row_state[row], flags);
+    }
+    __threadfence();
+    csync();
+    if (tid == 0) sm.last = (atomicAdd(&p.row_counter[row], 1u) == (uint32_t)(S - 1));
+    csync();
+    if (!sm.last) return;
+    __threadfence();
+    if (tid == 0) {
+        p.row_counter[row] = 0;
+        sm.flags = atomicExch(&p.row_state[row], 0u);
+        sm.cnt = 0;
+        sm.thr = -INFINITY;
+    }
+    csync();
+    const uint32_t rf = sm.flags;
+    if (!(rf & (FLAG_NAN | FLAG_OVERFLOW | FLAG_TIMEOUT))) {
+        for (int cc = 0; cc < S; ++cc) {
+            const int64_t sl = row * S + cc;
+            append_list(p.chunk_cand + sl * p.outcap, (int)__ldcg(p.chunk_count + sl), ckey, cidx, sm, k);
+        }
+    }
+    row_done(p, row, sm.flags | rf, region, sm);
 }
 
 template <bool TMA>
@@ -175,7 +272,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
                 sm.cnt = 0;
                 sm.thr = -INFINITY;
             }
-            __syncthreads();
+            csync();
             if (!(sm.flags & (FLAG_NAN | FLAG_OVERFLOW | FLAG_TIMEOUT))) {
                 for (int sh = 0; sh < p.nshards; ++sh) {
                     const int64_t sl = (int64_t)sh * p.rows + row;
@@ -206,7 +303,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
         fence_mbar_init();
         pol = policy_evict_first();
     }
-    __syncthreads();
+    csync();
     auto unit_tiles = [&](int64_t u) -> int {
         const int64_t t0 = (int64_t)(u % S) * TPC;
         return (int)min((int64_t)TPC, NTL - t0);
@@ -235,6 +332,8 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
         for (int s = 0; s < STAGES; ++s) issue();
 
     uint32_t cseq = 0;
+    const int trig = min(CAP / 2, max(512, 4 * k));
+    MXS_PROF_T0(ttot);
     for (int64_t j = 0; j < nj; ++j) {
         const int64_t u = blockIdx.x + j * G;
         const int64_t row = u / S;
@@ -246,17 +345,11 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
             sm.thr = -INFINITY;
             sm.flags = 0;
         }
-        __syncthreads();
+        csync();
         int nan = 0;
-        for (int t = 0; t < nt; ++t) {
-            const int64_t a = ((int64_t)c * TPC + t) * TILE;
-            const int len = (int)(min(a + TILE, V) - a);
-            const int bulk_n = len & ~3;
-            const int s = cseq % STAGES;
-            if (TMA) {
-                if (!mbar_wait_bounded(&sm.bar[s], (cseq / STAGES) & 1)) atomicOr(&sm.flags, FLAG_TIMEOUT);
-            }
-            const float* st = ring + s * TILE;
+        // Tile in checked sub-steps of SUB logits (partial tiles, the plain-load
+        // variant, and re-scans after an overflow).
+        auto slow_tile = [&](const float* st, const float* xr, int64_t a, int len, int bulk_n) {
             for (int sub = 0; sub * SUB < len; ++sub) {
                 const int off = sub * SUB + tid * 4;
                 float v[4];
@@ -289,62 +382,365 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
                     idx[q] = (int32_t)(a + off + q);
                 }
                 block_append4(ckey, cidx, sm, m, key, idx);
-                __syncthreads();
+                csync();
                 const int cnt = sm.cnt;
-                if (cnt > CAP - SUB) shrink_candidates(ckey, cidx, sm, cnt, k);
+                if (cnt > CAP - SUB) {
+                    MXS_PROF_T0(ts);
+                    shrink_candidates(ckey, cidx, sm, cnt, k);
+                    MXS_PROF_ADD(2, ts);
+                }
             }
+        };
+        for (int t = 0; t < nt; ++t) {
+            const int64_t a = ((int64_t)c * TPC + t) * TILE;
+            const int len = (int)(min(a + TILE, V) - a);
+            const int bulk_n = len & ~3;
+            const int s = cseq % STAGES;
+            MXS_PROF_T0(tw);
+            if (TMA) {
+                if (!mbar_wait_bounded(&sm.bar[s], (cseq / STAGES) & 1)) atomicOr(&sm.flags, FLAG_TIMEOUT);
+            }
+            MXS_PROF_ADD(0, tw);
+            MXS_PROF_T0(tc);
+            const float* st = ring + s * TILE;
+            if (TMA && len == TILE) {
+                // Whole tile in shared memory: 16 logits per thread, one sync.
+                const float4* st4 = reinterpret_cast<const float4*>(st);
+                float4 f[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) f[q] = st4[tid + NT * q];
+                float thr = sm.thr;
+                if (t == 0 && k <= NT) {
+                    // Seed the threshold with the k-th largest of the 256
+                    // per-thread maxima: k distinct logits are >= it, so it
+                    // cannot exceed the unit's k-th largest value.
+                    float mx = -INFINITY;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        mx = f[q].x > mx ? f[q].x : mx;
+                        mx = f[q].y > mx ? f[q].y : mx;
+                        mx = f[q].z > mx ? f[q].z : mx;
+                        mx = f[q].w > mx ? f[q].w : mx;
+                    }
+                    ckey[tid] = fkey(mx);  // the buffer is empty at a unit's first tile
+                    csync();
+                    thr = fkey_inv(block_select_kth(ckey, NT, k, sm));
+                    if (tid == 0) sm.thr = thr;
+                }
+                const int cnt0 = sm.cnt;
+                uint32_t m16 = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float vv[4] = {f[q].x, f[q].y, f[q].z, f[q].w};
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        nan |= (vv[c4] != vv[c4]);
+                        if (vv[c4] >= thr) m16 |= 1u << (4 * q + c4);
+                    }
+                }
+                block_append16(ckey, cidx, sm, m16, f, (int32_t)(a + 4 * tid));
+                csync();
+                const int cnt = sm.cnt;
+                if (cnt > CAP) {
+                    // Entries were lost: drop this tile's, raise the threshold,
+                    // and take the tile again in checked sub-steps.
+                    csync();
+                    if (tid == 0) sm.cnt = cnt0;
+                    csync();
+                    if (cnt0 > 0) shrink_candidates(ckey, cidx, sm, cnt0, k);
+                    slow_tile(st, xr, a, len, bulk_n);
+                } else if (cnt > trig) {
+                    MXS_PROF_T0(ts);
+                    shrink_candidates(ckey, cidx, sm, cnt, k);
+                    MXS_PROF_ADD(2, ts);
+                }
+            } else {
+                slow_tile(st, xr, a, len, bulk_n);
+            }
+            MXS_PROF_ADD(1, tc);
             if (TMA && tid == 0) {
                 fence_proxy_async_smem();
                 issue();
             }
             ++cseq;
         }
-        uint32_t flags = sm.flags | (__syncthreads_or(nan) ? FLAG_NAN : 0u);
-        if (S == 1) {
-            row_done(p, row, flags, region, sm);
-            continue;
-        }
-        // S > 1: publish this chunk's candidates >= its k-th largest key; the
-        // last chunk of the row to finish merges them and finishes the row.
-        int cnt = sm.cnt;
-        if (!(flags & (FLAG_NAN | FLAG_OVERFLOW | FLAG_TIMEOUT)) && cnt > k) {
-            const uint32_t kth = block_select_kth(ckey, cnt, k, sm);
-            cnt = block_compact_ge(ckey, cidx, sm, cnt, kth);
-        }
-        if (cnt > p.outcap) flags |= FLAG_OVERFLOW;
-        const int64_t slot = row * S + c;
-        if (!(flags & FLAG_OVERFLOW)) {
-            uint64_t* dst = p.chunk_cand + slot * p.outcap;
-            for (int i = tid; i < cnt; i += NT) dst[i] = ((uint64_t)ckey[i] << 32) | (uint32_t)cidx[i];
-        }
-        if (tid == 0) {
-            p.chunk_count[slot] = (uint32_t)cnt;
-            if (flags) atomicOr(&p.row_state[row], flags);
-        }
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) sm.last = (atomicAdd(&p.row_counter[row], 1u) == (uint32_t)(S - 1));
-        __syncthreads();
-        if (!sm.last) continue;
-        __threadfence();
-        if (tid == 0) {
-            p.row_counter[row] = 0;
-            sm.flags = atomicExch(&p.row_state[row], 0u);
-            sm.cnt = 0;
-            sm.thr = -INFINITY;
-        }
-        __syncthreads();
-        const uint32_t rf = sm.flags;
-        if (!(rf & (FLAG_NAN | FLAG_OVERFLOW | FLAG_TIMEOUT))) {
-            for (int cc = 0; cc < S; ++cc) {
-                const int64_t sl = row * S + cc;
-                append_list(p.chunk_cand + sl * p.outcap, (int)__ldcg(p.chunk_count + sl), ckey, cidx, sm, k);
-            }
-        }
-        row_done(p, row, sm.flags | rf, region, sm);
+        const uint32_t flags = sm.flags | (csync_or(nan) ? FLAG_NAN : 0u);
+        MXS_PROF_T0(tf);
+        unit_end(p, row, c, flags, region, sm);
+        MXS_PROF_ADD(3, tf);
     }
+    MXS_PROF_ADD(7, ttot);
     if (TMA && tid == 0)
         for (int s = 0; s < STAGES; ++s) mbar_inval(&sm.bar[s]);
+}
+
+#ifdef MXS_PROFILE
+extern "C" __attribute__((visibility("default"))) int mxs_prof_read(unsigned long long* host, int clear) {
+    if (cudaMemcpyFromSymbol(host, g_mxs_prof, sizeof(g_mxs_prof)) != cudaSuccess) return -3;
+    if (clear) {
+        static unsigned long long zeros[PROF_CTAS][PROF_PHASES];
+        if (cudaMemcpyToSymbol(g_mxs_prof, zeros, sizeof(zeros)) != cudaSuccess) return -3;
+    }
+    return 0;
+}
+#endif
+
+
+// ---------------------------------------------------------------------------
+// Warp-specialised streaming kernel (aligned rows, k <= KWS): warp 8 is the
+// producer, issuing one bulk copy per TILE into a STAGES ring (stage full /
+// stage empty mbarriers); warps 0-7 each filter a 512-logit slice of every tile
+// into a private candidate buffer, without any CTA-wide barrier while a unit
+// streams. A warp whose buffer passes WTRIG selects its own k-th largest key
+// (k entries of the unit are >= it, so it is a valid lower bound for the whole
+// unit), compacts, and publishes it with atomicMax; every warp filters against
+// the highest bound published.
+// ---------------------------------------------------------------------------
+
+// Raise the warp's bound to the k-th largest key it holds and drop the rest.
+__device__ __forceinline__ void warp_shrink(uint32_t* wk, int32_t* wi, int& wcnt, float& wthr, int k,
+                                            uint32_t* hist, Misc& sm) {
+    if (wcnt < k) return;
+    const uint32_t kth = warp_select_kth(wk, wcnt, k, hist);
+    wcnt = warp_compact_ge(wk, wi, wcnt, kth);
+    wthr = fkey_inv(kth);
+    if ((threadIdx.x & 31) == 0) atomicMax(&sm.thr_key, kth);
+}
+
+// Append this lane's passing logits (bit b of m: value vv[b], column
+// col[b/4] + b%4) to the warp buffer; returns false, appending nothing, when
+// they do not all fit.
+__device__ __forceinline__ bool warp_append(uint32_t* wk, int32_t* wi, int& wcnt, uint32_t m, const float (&vv)[16],
+                                            const int32_t (&col)[4]) {
+    const int c = __popc(m);
+    const int incl = warp_incl_scan(c);
+    const int tot = __shfl_sync(0xffffffffu, incl, 31);
+    if (tot == 0) return true;
+    if (wcnt + tot > WCAP) return false;
+    int pos = wcnt + incl - c;
+#pragma unroll
+    for (int b = 0; b < 16; ++b) {
+        if (m & (1u << b)) {
+            wk[pos] = fkey(vv[b]);
+            wi[pos] = col[b >> 2] + (b & 3);
+            ++pos;
+        }
+    }
+    wcnt += tot;
+    return true;
+}
+
+__global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    float* ring = reinterpret_cast<float*>(smem);
+    unsigned char* region = smem + RING_BYTES;
+    uint32_t* ckey = reinterpret_cast<uint32_t*>(region);
+    int32_t* cidx = reinterpret_cast<int32_t*>(region + CAP * 4);
+    Misc& sm = *reinterpret_cast<Misc*>(region + REGION_BYTES);
+    uint32_t* whist_all = reinterpret_cast<uint32_t*>(smem + SMEM_BYTES);
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int k = p.k_use;
+    const int64_t V = p.vocab;
+    const int64_t G = gridDim.x;
+    const int64_t nj = (p.units > (int64_t)blockIdx.x) ? (p.units - blockIdx.x + G - 1) / G : 0;
+    const int S = p.S, TPC = p.tiles_per_chunk;
+    const int64_t NTL = (V + TILE - 1) / TILE;
+    auto unit_tiles = [&](int64_t u) -> int {
+        const int64_t t0 = (int64_t)(u % S) * TPC;
+        return (int)min((int64_t)TPC, NTL - t0);
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&sm.bar[s], 1);
+            mbar_init(&sm.ebar[s], NWARPS);
+        }
+        sm.flags = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == NWARPS) {
+        // Producer warp: lane 0 streams every tile of every unit of this CTA.
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            uint32_t seq = 0;
+            bool ok = true;
+            for (int64_t j = 0; j < nj && ok; ++j) {
+                const int64_t u = blockIdx.x + j * G;
+                const int64_t row = u / S;
+                const int nt = unit_tiles(u);
+                for (int t = 0; t < nt; ++t, ++seq) {
+                    const int s = seq % STAGES;
+                    if (seq >= STAGES && !mbar_wait_bounded(&sm.ebar[s], ((seq / STAGES) - 1) & 1)) {
+                        atomicOr(&sm.flags, FLAG_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
+                    const int64_t a = ((int64_t)(u % S) * TPC + t) * TILE;
+                    const int64_t b = min(a + TILE, V);
+                    const uint32_t bytes = (uint32_t)(((b - a) & ~int64_t(3)) * 4);
+                    if (bytes) {
+                        mbar_arrive_expect_tx(&sm.bar[s], bytes);
+                        bulk_g2s(ring + s * TILE, p.logits + row * p.ld + a, bytes, &sm.bar[s], pol);
+                    } else {
+                        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.bar[s])) : "memory");
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    uint32_t* wk = ckey + warp * WCAP;
+    int32_t* wi = cidx + warp * WCAP;
+    uint32_t* whist = whist_all + warp * 256;
+    uint32_t cseq = 0;
+    MXS_PROF_T0(ttot);
+    for (int64_t j = 0; j < nj; ++j) {
+        const int64_t u = blockIdx.x + j * G;
+        const int64_t row = u / S;
+        const int c = (int)(u % S);
+        const int nt = unit_tiles(u);
+        const float* xr = p.logits + row * p.ld;
+        csync();  // the previous unit is finished by every consumer thread
+        if (tid == 0) {
+            sm.cnt = 0;
+            sm.thr = -INFINITY;
+            sm.thr_key = 0u;  // below every key of a non-NaN logit
+            atomicAnd(&sm.flags, FLAG_TIMEOUT);  // a producer timeout stays; row flags start clear
+        }
+        csync();
+        int wcnt = 0, nan = 0;
+        bool stopped = false;
+        float wthr = -INFINITY;
+        for (int t = 0; t < nt; ++t, ++cseq) {
+            const int64_t a = ((int64_t)c * TPC + t) * TILE;
+            const int len = (int)(min(a + TILE, V) - a);
+            const int bulk_n = len & ~3;
+            const int s = cseq % STAGES;
+            MXS_PROF_T0(tw);
+            if (!mbar_wait_bounded(&sm.bar[s], (cseq / STAGES) & 1)) atomicOr(&sm.flags, FLAG_TIMEOUT);
+            MXS_PROF_ADD(0, tw);
+            MXS_PROF_T0(tc);
+            const float* st = ring + s * TILE;
+            // this lane's 4 groups of 4 logits: float4 slots warp*128 + lane + 32q
+            float vv[16];
+            int32_t col[4];
+            uint32_t valid = 0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int e0 = 4 * (warp * 128 + lane + 32 * q);
+                col[q] = (int32_t)(a + e0);
+                if (e0 + 4 <= bulk_n) {
+                    const float4 f = *reinterpret_cast<const float4*>(st + e0);
+                    vv[4 * q] = f.x; vv[4 * q + 1] = f.y; vv[4 * q + 2] = f.z; vv[4 * q + 3] = f.w;
+                    valid |= 0xFu << (4 * q);
+                } else {
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        const int e = e0 + c4;
+                        vv[4 * q + c4] = 0.f;
+                        if (e < len) {
+                            vv[4 * q + c4] = (e < bulk_n) ? st[e] : xr[a + e];
+                            valid |= 1u << (4 * q + c4);
+                        }
+                    }
+                }
+            }
+            // the stage's bytes are in registers: hand it back to the producer
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.ebar[s])) : "memory");
+            if (t == 0) {
+                // Seed: the k-th largest of the 256 per-lane maxima of the
+                // unit's first tile (k <= KWS distinct logits are >= it).
+                float mx = -INFINITY;
+#pragma unroll
+                for (int b = 0; b < 16; ++b)
+                    if ((valid >> b) & 1u) mx = vv[b] > mx ? vv[b] : mx;
+                ckey[tid] = fkey(mx);
+                csync();
+                const uint32_t kth = block_select_kth(ckey, NT, k, sm);
+                if (tid == 0) sm.thr_key = kth;
+                csync();
+            }
+            if (!stopped) {
+                const uint32_t tk = *reinterpret_cast<volatile uint32_t*>(&sm.thr_key);
+                float thr = fkey_inv(tk);
+                thr = thr > wthr ? thr : wthr;
+                uint32_t m = 0;
+#pragma unroll
+                for (int b = 0; b < 16; ++b) {
+                    nan |= (((valid >> b) & 1u) && vv[b] != vv[b]);
+                    if (((valid >> b) & 1u) && vv[b] >= thr) m |= 1u << b;
+                }
+                if (!warp_append(wk, wi, wcnt, m, vv, col)) {
+                    // does not fit: raise the bound, filter again, and give up
+                    // (massive ties: the exact replay takes the row) if it still does not fit
+                    warp_shrink(wk, wi, wcnt, wthr, k, whist, sm);
+                    const uint32_t tk2 = *reinterpret_cast<volatile uint32_t*>(&sm.thr_key);
+                    float thr2 = fkey_inv(tk2);
+                    thr2 = thr2 > wthr ? thr2 : wthr;
+                    m = 0;
+#pragma unroll
+                    for (int b = 0; b < 16; ++b)
+                        if (((valid >> b) & 1u) && vv[b] >= thr2) m |= 1u << b;
+                    if (!warp_append(wk, wi, wcnt, m, vv, col)) {
+                        stopped = true;
+                        if (lane == 0) atomicOr(&sm.flags, FLAG_OVERFLOW);
+                    }
+                }
+                if (wcnt > WTRIG) {
+                    MXS_PROF_T0(ts);
+                    warp_shrink(wk, wi, wcnt, wthr, k, whist, sm);
+                    MXS_PROF_ADD(2, ts);
+                }
+            } else {
+#pragma unroll
+                for (int b = 0; b < 16; ++b) nan |= (((valid >> b) & 1u) && vv[b] != vv[b]);
+            }
+            MXS_PROF_ADD(1, tc);
+        }
+        // Gather the warp buffers (entries >= the final bound) into ckey/cidx[0, cnt).
+        csync();
+        const uint32_t fin = sm.thr_key;
+        constexpr int PER = WCAP / 32;
+        uint32_t kk[PER];
+        int32_t ii[PER];
+        uint32_t keep = 0;
+#pragma unroll
+        for (int r = 0; r < PER; ++r) {
+            const int i = lane + 32 * r;
+            kk[r] = 0;
+            ii[r] = 0;
+            if (i < wcnt) {
+                kk[r] = wk[i];
+                ii[r] = wi[i];
+                if (kk[r] >= fin) keep |= 1u << r;
+            }
+        }
+        int total;
+        const int off = block_excl_scan(__popc(keep), sm, &total);  // (ends with a CTA sync)
+        int pos = off;
+#pragma unroll
+        for (int r = 0; r < PER; ++r) {
+            if (keep & (1u << r)) {
+                ckey[pos] = kk[r];
+                cidx[pos] = ii[r];
+                ++pos;
+            }
+        }
+        if (tid == 0) {
+            sm.cnt = total;
+            sm.thr = fkey_inv(fin);
+        }
+        const uint32_t flags = sm.flags | (csync_or(nan) ? FLAG_NAN : 0u);
+        MXS_PROF_T0(tf);
+        unit_end(p, row, c, flags, region, sm);
+        MXS_PROF_ADD(3, tf);
+    }
+    MXS_PROF_ADD(7, ttot);
 }
 
 // ---------------------------------------------------------------------------
@@ -358,11 +754,21 @@ cudaError_t sample_kernel_configure(int* blocks_per_sm) {
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(sample_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, sample_kernel<true>, NT, SMEM_BYTES);
+    e = cudaFuncSetAttribute(sample_kernel_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES_WS);
+    if (e != cudaSuccess) return e;
+    int a = 0, b = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, sample_kernel<true>, NT, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, sample_kernel_ws, NT_WS, SMEM_BYTES_WS);
+    if (e != cudaSuccess) return e;
+    *blocks_per_sm = a < b ? a : b;
+    return cudaSuccess;
 }
 
 cudaError_t sample_kernel_launch(const Params& p, int grid, bool tma, cudaStream_t stream) {
-    if (tma)
+    if (tma && p.mode != MODE_MERGE && p.k_use <= KWS && !p.force_block_path)
+        sample_kernel_ws<<<grid, NT_WS, SMEM_BYTES_WS, stream>>>(p);
+    else if (tma)
         sample_kernel<true><<<grid, NT, SMEM_BYTES, stream>>>(p);
     else
         sample_kernel<false><<<grid, NT, SMEM_BYTES, stream>>>(p);

@@ -70,6 +70,8 @@ struct Params {
     const uint32_t* in_count;  // MODE_MERGE: nshards x rows
     const uint32_t* in_flags;  // MODE_MERGE: nshards x rows (nullable)
     int nshards, in_cap;
+    int force_block_path;      // 1: use the CTA-synchronous streaming kernel even where the
+                               // warp-specialised one applies (tests cover both)
 };
 constexpr int MODE_SAMPLE = 0;
 constexpr int MODE_EMIT = 1;
@@ -79,9 +81,12 @@ constexpr int MODE_MERGE = 2;
 // candidate buffer (keys | indices), the sort buffer + probabilities, or the
 // exact path's heap + replay list, then small scalars.
 struct Misc {
-    uint64_t bar[STAGES];
+    uint64_t bar[STAGES];   // stage full (bytes landed)
+    uint64_t ebar[STAGES];  // stage empty (every consumer warp is done with it)
+    uint32_t thr_key;       // running threshold key shared by the consumer warps
     uint32_t hist[256];
     int warp_tot[NWARPS];
+    uint32_t warp_or[NWARPS];
     int cnt;
     float thr;
     uint32_t digit;
@@ -95,6 +100,14 @@ struct Misc {
 constexpr size_t RING_BYTES = size_t(STAGES) * TILE * sizeof(float);
 constexpr size_t REGION_BYTES = size_t(CAP) * 8;
 constexpr size_t SMEM_BYTES = RING_BYTES + REGION_BYTES + sizeof(Misc);
+// Warp-specialised variant: 8 consumer warps + 1 producer warp; each consumer
+// warp owns WCAP entries of the candidate region and a 256-bin histogram.
+constexpr int KWS = 128;                 // largest k of the warp-specialised path
+constexpr int NT_WS = NT + 32;
+constexpr int WCAP = CAP / NWARPS;       // 512 candidates per warp
+constexpr int WTRIG = WCAP / 2;          // shrink a warp buffer past this
+constexpr size_t WHIST_BYTES = size_t(NWARPS) * 256 * 4;
+constexpr size_t SMEM_BYTES_WS = SMEM_BYTES + WHIST_BYTES;
 static_assert(SORTMAX * 8 + KFAST * 8 <= REGION_BYTES, "sort + prob buffers exceed the region");
 static_assert(HEAP_SMEM_MAX * 8 + XTILE * 8 <= REGION_BYTES, "heap + replay list exceed the region");
 
@@ -126,31 +139,112 @@ __device__ __forceinline__ void block_append4(uint32_t* ckey, int32_t* cidx, Mis
     }
 }
 
-// k-th largest key among ckey[0, cnt), 1 <= k <= cnt: four 8-bit digit passes.
+// Append the logits of a 16-logit group (bit 4q+c of m set = component c of
+// f[q] passes; its column is i0 + 4*NT*q + c), warp-aggregated.
+__device__ __forceinline__ void block_append16(uint32_t* ckey, int32_t* cidx, Misc& sm, uint32_t m,
+                                               const float4 (&f)[4], int32_t i0) {
+    const int c = __popc(m);
+    if (!__any_sync(0xffffffffu, c)) return;
+    const int lane = threadIdx.x & 31;
+    const int incl = warp_incl_scan(c);
+    int base = 0;
+    if (lane == 31 && incl) base = atomicAdd(&sm.cnt, incl);
+    base = __shfl_sync(0xffffffffu, base, 31);
+    int pos = base + incl - c;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float vv[4] = {f[q].x, f[q].y, f[q].z, f[q].w};
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+            if (m & (1u << (4 * q + c4))) {
+                if (pos < CAP) {
+                    ckey[pos] = fkey(vv[c4]);
+                    cidx[pos] = i0 + 4 * NT * q + c4;
+                }
+                ++pos;
+            }
+        }
+    }
+}
+
+// AND and OR of all keys in ckey[0, cnt) (block-wide).
+__device__ __forceinline__ void block_and_or(const uint32_t* ckey, int cnt, Misc& sm, uint32_t* a_out,
+                                             uint32_t* o_out) {
+    uint32_t a = ~0u, o = 0u;
+    for (int i = threadIdx.x; i < cnt; i += NT) {
+        const uint32_t key = ckey[i];
+        a &= key;
+        o |= key;
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+        a &= __shfl_xor_sync(0xffffffffu, a, d);
+        o |= __shfl_xor_sync(0xffffffffu, o, d);
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        sm.warp_tot[w] = (int)a;
+        sm.warp_or[w] = o;
+    }
+    csync();
+    a = ~0u;
+    o = 0u;
+#pragma unroll
+    for (int i = 0; i < NWARPS; ++i) {
+        a &= (uint32_t)sm.warp_tot[i];
+        o |= sm.warp_or[i];
+    }
+    csync();
+    *a_out = a;
+    *o_out = o;
+}
+
+// k-th largest key among ckey[0, cnt), 1 <= k <= cnt. Radix select from the
+// most significant bit in which the keys differ, at most 8 bits per pass; lanes
+// of a warp that hit the same bin add once (match_any), so a narrow key range
+// does not serialise the shared-memory atomics.
 __device__ inline uint32_t block_select_kth(const uint32_t* ckey, int cnt, int k, Misc& sm) {
-    const int tid = threadIdx.x;
-    uint32_t prefix = 0, mask = 0;
+    const int tid = threadIdx.x, lane = tid & 31;
+    uint32_t a, o;
+    block_and_or(ckey, cnt, sm, &a, &o);
+    const uint32_t diff = a ^ o;
+    if (diff == 0) return a;  // all keys equal
+    int hi = 31 - __clz(diff);  // highest undecided bit
+    uint32_t prefix = a & ~((2u << hi) - 1u);
+    uint32_t mask = ~((2u << hi) - 1u);
     int krem = k;
 #pragma unroll 1
-    for (int shift = 24; shift >= 0; shift -= 8) {
+    while (hi >= 0) {
+        const int w = min(8, hi + 1);
+        const int shift = hi + 1 - w;
+        const int nb = 1 << w;
         sm.hist[tid] = 0;
-        __syncthreads();
-        for (int i = tid; i < cnt; i += NT) {
-            const uint32_t key = ckey[i];
-            if ((key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255u], 1u);
+        csync();
+        for (int i0 = 0; i0 < cnt; i0 += NT) {
+            const int i = i0 + tid;
+            int bin = -1;
+            if (i < cnt) {
+                const uint32_t key = ckey[i];
+                if ((key & mask) == prefix) bin = (int)((key >> shift) & (uint32_t)(nb - 1));
+            }
+            const uint32_t same = __match_any_sync(0xffffffffu, bin);
+            if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(&sm.hist[bin], (uint32_t)__popc(same));
         }
-        __syncthreads();
+        csync();
         if (tid < 32) {
-            // lane l owns bins 255-8l .. 248-8l, scanned from the top down
+            // lane l owns bins nb-1-l*per .. nb-per-l*per, scanned from the top down
+            const int per = (nb + 31) / 32;
             int own = 0;
-#pragma unroll
-            for (int b = 0; b < 8; ++b) own += (int)sm.hist[255 - 8 * tid - b];
+            for (int b = 0; b < per; ++b) {
+                const int bin = nb - 1 - lane * per - b;
+                if (bin >= 0) own += (int)sm.hist[bin];
+            }
             const int incl = warp_incl_scan(own);
             const int excl = incl - own;
             if (excl < krem && incl >= krem) {
                 int run = excl;
-                for (int b = 0; b < 8; ++b) {
-                    const int bin = 255 - 8 * tid - b;
+                for (int b = 0; b < per; ++b) {
+                    const int bin = nb - 1 - lane * per - b;
                     const int h = (int)sm.hist[bin];
                     if (run + h >= krem) {
                         sm.digit = (uint32_t)bin;
@@ -161,12 +255,148 @@ __device__ inline uint32_t block_select_kth(const uint32_t* ckey, int cnt, int k
                 }
             }
         }
-        __syncthreads();
+        csync();
         prefix |= sm.digit << shift;
-        mask |= 0xFFu << shift;
+        mask |= (uint32_t)(nb - 1) << shift;
         krem = sm.krem;
+        hi = shift - 1;
     }
     return prefix;
+}
+
+// ---------------------------------------------------------------------------
+// Warp primitives of the warp-specialised streaming path (one warp, no CTA sync).
+// ---------------------------------------------------------------------------
+
+// k-th largest key among keys[0, n), 1 <= k <= n, by one warp; hist: 256 words
+// private to the warp.
+__device__ inline uint32_t warp_select_kth(const uint32_t* keys, int n, int k, uint32_t* hist) {
+    const int lane = threadIdx.x & 31;
+    uint32_t a = ~0u, o = 0u;
+    for (int i = lane; i < n; i += 32) {
+        const uint32_t key = keys[i];
+        a &= key;
+        o |= key;
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+        a &= __shfl_xor_sync(0xffffffffu, a, d);
+        o |= __shfl_xor_sync(0xffffffffu, o, d);
+    }
+    const uint32_t diff = a ^ o;
+    if (diff == 0) return a;
+    int hi = 31 - __clz(diff);
+    uint32_t prefix = a & ~((2u << hi) - 1u);
+    uint32_t mask = ~((2u << hi) - 1u);
+    int krem = k;
+#pragma unroll 1
+    while (hi >= 0) {
+        const int w = min(8, hi + 1);
+        const int shift = hi + 1 - w;
+        const int nb = 1 << w;
+        for (int b = lane; b < 256; b += 32) hist[b] = 0;
+        __syncwarp();
+        for (int i0 = 0; i0 < n; i0 += 32) {
+            const int i = i0 + lane;
+            int bin = -1;
+            if (i < n) {
+                const uint32_t key = keys[i];
+                if ((key & mask) == prefix) bin = (int)((key >> shift) & (uint32_t)(nb - 1));
+            }
+            const uint32_t same = __match_any_sync(0xffffffffu, bin);
+            if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(same));
+        }
+        __syncwarp();
+        const int per = (nb + 31) / 32;
+        int own = 0;
+        for (int b = 0; b < per; ++b) {
+            const int bin = nb - 1 - lane * per - b;
+            if (bin >= 0) own += (int)hist[bin];
+        }
+        const int incl = warp_incl_scan(own);
+        const int excl = incl - own;
+        const bool mine = (excl < krem && incl >= krem);
+        int d = 0, kr = 0;
+        if (mine) {
+            int run = excl;
+            for (int b = 0; b < per; ++b) {
+                const int bin = nb - 1 - lane * per - b;
+                const int h = (int)hist[bin];
+                if (run + h >= krem) {
+                    d = bin;
+                    kr = krem - run;
+                    break;
+                }
+                run += h;
+            }
+        }
+        const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+        d = __shfl_sync(0xffffffffu, d, src);
+        kr = __shfl_sync(0xffffffffu, kr, src);
+        prefix |= (uint32_t)d << shift;
+        mask |= (uint32_t)(nb - 1) << shift;
+        krem = kr;
+        hi = shift - 1;
+        __syncwarp();
+    }
+    return prefix;
+}
+
+// Keep the entries of keys/idx[0, n) with key >= kth, in place, in order; one warp.
+__device__ __forceinline__ int warp_compact_ge(uint32_t* keys, int32_t* idx, int n, uint32_t kth) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t lt = (1u << lane) - 1u;
+    int out = 0;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        uint32_t kk = 0;
+        int32_t ii = 0;
+        bool keep = false;
+        if (i < n) {
+            kk = keys[i];
+            ii = idx[i];
+            keep = kk >= kth;
+        }
+        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+            const int pos = out + __popc(bal & lt);
+            keys[pos] = kk;
+            idx[pos] = ii;
+        }
+        out += __popc(bal);
+    }
+    __syncwarp();
+    return out;
+}
+
+// Sort 64 packed entries held two per lane (a0 = element lane, a1 = element
+// lane + 32) descending, with a register bitonic network (warp-synchronous).
+__device__ __forceinline__ void warp_sort64_desc(uint64_t& a0, uint64_t& a1) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride == 32) {
+                const bool desc = ((lane & size) == 0);
+                if ((a0 < a1) == desc) {
+                    const uint64_t t = a0;
+                    a0 = a1;
+                    a1 = t;
+                }
+            } else {
+#pragma unroll
+                for (int slot = 0; slot < 2; ++slot) {
+                    uint64_t& v = slot ? a1 : a0;
+                    const int i = lane + 32 * slot;
+                    const uint64_t o = __shfl_xor_sync(0xffffffffu, v, stride);
+                    const bool desc = ((i & size) == 0);
+                    const bool keep_max = (desc == ((i & stride) == 0));
+                    v = keep_max ? (v > o ? v : o) : (v < o ? v : o);
+                }
+            }
+        }
+    }
 }
 
 // Keep the candidates with key >= kth; returns the new count.
@@ -186,9 +416,9 @@ __device__ inline int block_compact_ge(uint32_t* ckey, int32_t* cidx, Misc& sm, 
             if (kk[r] >= kth) keep |= 1u << r;
         }
     }
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) sm.cnt = 0;
-    __syncthreads();
+    csync();
 #pragma unroll
     for (int r = 0; r < PER; r += 4) {
         const uint32_t m = (keep >> r) & 0xFu;
@@ -196,7 +426,7 @@ __device__ inline int block_compact_ge(uint32_t* ckey, int32_t* cidx, Misc& sm, 
         const int32_t i4[4] = {ii[r], ii[r + 1], ii[r + 2], ii[r + 3]};
         block_append4(ckey, cidx, sm, m, k4, i4);
     }
-    __syncthreads();
+    csync();
     return sm.cnt;
 }
 
@@ -220,7 +450,7 @@ __device__ inline void block_sort_desc(uint64_t* a, int P) {
                 }
             }
         }
-        __syncthreads();
+        csync();
         return;
     }
     for (int size = 2; size <= P; size <<= 1) {
@@ -235,7 +465,7 @@ __device__ inline void block_sort_desc(uint64_t* a, int P) {
                     a[hi] = x;
                 }
             }
-            __syncthreads();
+            csync();
         }
     }
 }
@@ -246,7 +476,7 @@ __device__ __forceinline__ int block_excl_scan(int v, Misc& sm, int* total) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int incl = warp_incl_scan(v);
     if (lane == 31) sm.warp_tot[w] = incl;
-    __syncthreads();
+    csync();
     int off = 0, tot = 0;
 #pragma unroll
     for (int i = 0; i < NWARPS; ++i) {
@@ -254,7 +484,7 @@ __device__ __forceinline__ int block_excl_scan(int v, Misc& sm, int* total) {
         off += (i < w) ? t : 0;
         tot += t;
     }
-    __syncthreads();
+    csync();
     *total = tot;
     return off + incl - v;
 }

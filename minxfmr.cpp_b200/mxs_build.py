@@ -12,6 +12,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(OUT_DIR, "libmxs.so")
+# phase-timer build (-DMXS_PROFILE) for kernel analysis; never loaded by the product path
+PROF_LIB = os.path.join(OUT_DIR, "libmxs_prof.so")
 SOURCES = ["mxs_sampler.cu", "mxs_api.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
@@ -24,22 +26,23 @@ FLAGS = [
 ]
 
 
-def build(verbose=False, force=False):
+def build(verbose=False, force=False, profile=False):
+    lib = PROF_LIB if profile else LIB
     os.makedirs(OUT_DIR, exist_ok=True)
     deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)] + [
         os.path.join(HERE, "..", "include", "mxs_sampler.h")]
-    if (not force and os.path.exists(LIB)
-            and os.path.getmtime(LIB) >= max(os.path.getmtime(d) for d in deps)):
-        return LIB
-    cmd = [NVCC] + FLAGS + (["-Xptxas", "-v"] if verbose else []) + \
-        [os.path.join(CSRC, s) for s in SOURCES] + ["-o", LIB]
+    if (not force and os.path.exists(lib)
+            and os.path.getmtime(lib) >= max(os.path.getmtime(d) for d in deps)):
+        return lib
+    cmd = [NVCC] + FLAGS + (["-Xptxas", "-v"] if verbose else []) + (["-DMXS_PROFILE"] if profile else []) + \
+        [os.path.join(CSRC, s) for s in SOURCES] + ["-o", lib]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if verbose or r.returncode:
         sys.stderr.write(r.stdout + r.stderr)
     if r.returncode:
-        raise RuntimeError("nvcc failed building libmxs.so")
-    return LIB
+        raise RuntimeError(f"nvcc failed building {lib}")
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(verbose="--verbose" in sys.argv, force=True))
+    print(build(verbose="--verbose" in sys.argv, force=True, profile="--profile" in sys.argv))

@@ -14,6 +14,17 @@ from test_oracle import GOLDEN_CASES, check_against_golden, golden_logits
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(params=["warp_specialised", "block_sync"], autouse=True)
+def kernel_variant(request, monkeypatch):
+    """Run every parity case on both streaming kernels."""
+    if request.param == "block_sync":
+        monkeypatch.setenv("MXS_SAMPLER_BLOCK_PATH", "1")
+    else:
+        monkeypatch.delenv("MXS_SAMPLER_BLOCK_PATH", raising=False)
+    return request.param
+
+
 RTOL = 1e-6
 
 
@@ -77,6 +88,8 @@ def test_config5_throughput_shapes(mxs, rows):
     u = oracle_lib.uniforms(105, rows)
     got = run_gpu(mxs, x, 0.8, 50, u)
     assert_parity(x, 0.8, 50, u, got, name=f"c5 rows={rows}")
+    # tie-free N(0, 2^2) rows must stay on the streaming path, not the replay
+    assert ((got[3] & mxs.ROW_EXACT) != 0).mean() <= 0.01
 
 
 def test_ragged_vocab_strided_and_unaligned(mxs):
