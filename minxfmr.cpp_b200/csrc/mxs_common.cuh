@@ -133,6 +133,21 @@ __device__ __forceinline__ int csync_or(int pred) {
     return r;
 }
 
+// max that returns NaN when either input is NaN (PTX max.NaN, sm_80+): one
+// reduction both screens 16 logits against the threshold and detects a NaN.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+__device__ __forceinline__ float max16_nan(const float4 (&f)[4]) {
+    const float a = fmax_nan(fmax_nan(f[0].x, f[0].y), fmax_nan(f[0].z, f[0].w));
+    const float b = fmax_nan(fmax_nan(f[1].x, f[1].y), fmax_nan(f[1].z, f[1].w));
+    const float c = fmax_nan(fmax_nan(f[2].x, f[2].y), fmax_nan(f[2].z, f[2].w));
+    const float d = fmax_nan(fmax_nan(f[3].x, f[3].y), fmax_nan(f[3].z, f[3].w));
+    return fmax_nan(fmax_nan(a, b), fmax_nan(c, d));
+}
+
 // Warp-inclusive prefix sum.
 __device__ __forceinline__ int warp_incl_scan(int v) {
     const int lane = threadIdx.x & 31;

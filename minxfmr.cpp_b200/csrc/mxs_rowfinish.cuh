@@ -22,6 +22,22 @@ __device__ __forceinline__ int lower_bound_cp(const double* cp, int n, double u)
     return first;
 }
 
+// ((p[0] + p[1]) + p[2]) + ... in this order (the reference's running sum),
+// with the loads of each block of 8 issued together.
+__device__ __forceinline__ double seq_sum(const double* p, int n) {
+    double s = 0.0;
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {
+        double v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = p[i + j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += v[j];
+    }
+    for (; i < n; ++i) s += p[i];
+    return s;
+}
+
 // e[0, k): the row's top-k in the reference's order. pbuf: k doubles.
 // Follows src/api/minxfmr.cpp:2104-2169 and libstdc++'s discrete_distribution
 // (bits/random.tcc:2657-2714): each double operation of the reference happens
@@ -38,11 +54,7 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
         const double maxs = (double)e[0].v;
         for (int i = tid; i < k; i += NT) pbuf[i] = exp(((double)e[i].v - maxs) / T);
         csync();
-        if (tid == 0) {
-            double s = 0.0;
-            for (int i = 0; i < k; ++i) s += pbuf[i];
-            sm.sum = s;
-        }
+        if (tid == 0) sm.sum = seq_sum(pbuf, k);
         csync();
         sum = sm.sum;
         greedy = (sum <= 0.0);
@@ -90,10 +102,7 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
                 for (int i = 0; i < n; ++i) pbuf[i] /= renorm;
         }
         sm.krem = n;
-        double s2 = 0.0;
-        if (n >= 2)
-            for (int i = 0; i < n; ++i) s2 += pbuf[i];
-        sm.sum = s2;
+        sm.sum = (n >= 2) ? seq_sum(pbuf, n) : 0.0;
     }
     csync();
     const int n = sm.krem;
@@ -107,7 +116,18 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
     csync();
     if (tid == 0) {
         double run = 0.0;
-        for (int i = 0; i < n; ++i) {
+        int i = 0;
+        for (; i + 8 <= n; i += 8) {  // loads of a block of 8 issue together; the adds stay in order
+            double v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = pbuf[i + j];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                run += v[j];
+                pbuf[i + j] = run;
+            }
+        }
+        for (; i < n; ++i) {
             run += pbuf[i];
             pbuf[i] = run;
         }
@@ -148,22 +168,26 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
                 for (int64_t j = k; j < V; ++j) heap_offer(h, k, Ent{x[j], (int32_t)j});
             csync();
         } else {
+            // Steps grow from NT to XTILE logits: the root starts as the
+            // smallest of the first k logits and rises fast, so short early
+            // steps keep the serial offers near k * (1 + ln(V / k)).
             constexpr int PER = XTILE / NT;
-            for (int64_t base = k; base < V; base += XTILE) {
+            int per = 1;
+            for (int64_t base = k; base < V; base += (int64_t)per * NT, per = per < PER ? 2 * per : PER) {
                 const float r0 = h[0].v;
                 float xv[PER];
                 int c = 0;
 #pragma unroll
                 for (int q = 0; q < PER; ++q) {
-                    const int64_t j = base + (int64_t)tid * PER + q;
-                    xv[q] = (j < V) ? x[j] : r0;
+                    const int64_t j = base + (int64_t)tid * per + q;
+                    xv[q] = (q < per && j < V) ? x[j] : r0;
                     c += (xv[q] > r0) ? 1 : 0;
                 }
                 int total;
                 int pos = block_excl_scan(c, sm, &total);
 #pragma unroll
                 for (int q = 0; q < PER; ++q) {
-                    if (xv[q] > r0) xl[pos++] = Ent{xv[q], (int32_t)(base + (int64_t)tid * PER + q)};
+                    if (xv[q] > r0) xl[pos++] = Ent{xv[q], (int32_t)(base + (int64_t)tid * per + q)};
                 }
                 csync();
                 if (tid == 0)

@@ -428,17 +428,21 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
                     if (tid == 0) sm.thr = thr;
                 }
                 const int cnt0 = sm.cnt;
-                uint32_t m16 = 0;
+                // max.NaN screen: NaN in any of the 16 flags the row (the exact
+                // replay takes it); otherwise only lanes whose max passes build bits
+                const float mxn = max16_nan(f);
+                nan |= (mxn != mxn);
+                if (__any_sync(0xffffffffu, mxn >= thr)) {
+                    uint32_t m16 = 0;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float vv[4] = {f[q].x, f[q].y, f[q].z, f[q].w};
+                    for (int q = 0; q < 4; ++q) {
+                        const float vv[4] = {f[q].x, f[q].y, f[q].z, f[q].w};
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) {
-                        nan |= (vv[c4] != vv[c4]);
-                        if (vv[c4] >= thr) m16 |= 1u << (4 * q + c4);
+                        for (int c4 = 0; c4 < 4; ++c4)
+                            if (vv[c4] >= thr) m16 |= 1u << (4 * q + c4);
                     }
+                    block_append16(ckey, cidx, sm, m16, f, (int32_t)(a + 4 * tid));
                 }
-                block_append16(ckey, cidx, sm, m16, f, (int32_t)(a + 4 * tid));
                 csync();
                 const int cnt = sm.cnt;
                 if (cnt > CAP) {
@@ -507,29 +511,6 @@ __device__ __forceinline__ void warp_shrink(uint32_t* wk, int32_t* wi, int& wcnt
     if ((threadIdx.x & 31) == 0) atomicMax(&sm.thr_key, kth);
 }
 
-// Append this lane's passing logits (bit b of m: value vv[b], column
-// col[b/4] + b%4) to the warp buffer; returns false, appending nothing, when
-// they do not all fit.
-__device__ __forceinline__ bool warp_append(uint32_t* wk, int32_t* wi, int& wcnt, uint32_t m, const float (&vv)[16],
-                                            const int32_t (&col)[4]) {
-    const int c = __popc(m);
-    const int incl = warp_incl_scan(c);
-    const int tot = __shfl_sync(0xffffffffu, incl, 31);
-    if (tot == 0) return true;
-    if (wcnt + tot > WCAP) return false;
-    int pos = wcnt + incl - c;
-#pragma unroll
-    for (int b = 0; b < 16; ++b) {
-        if (m & (1u << b)) {
-            wk[pos] = fkey(vv[b]);
-            wi[pos] = col[b >> 2] + (b & 3);
-            ++pos;
-        }
-    }
-    wcnt += tot;
-    return true;
-}
-
 __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
     extern __shared__ __align__(128) unsigned char smem[];
     float* ring = reinterpret_cast<float*>(smem);
@@ -596,6 +577,9 @@ __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
     uint32_t* wk = ckey + warp * WCAP;
     int32_t* wi = cidx + warp * WCAP;
     uint32_t* whist = whist_all + warp * 256;
+    // shrink a warp buffer once it holds 2k entries (at least 64): the bound
+    // then rises every ~k appended logits
+    const int wtrig = min(WTRIG, max(2 * k, 64));
     uint32_t cseq = 0;
     MXS_PROF_T0(ttot);
     for (int64_t j = 0; j < nj; ++j) {
@@ -627,79 +611,99 @@ __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
             const float* st = ring + s * TILE;
             // this lane's 4 groups of 4 logits: float4 slots warp*128 + lane + 32q
             float vv[16];
-            int32_t col[4];
-            uint32_t valid = 0;
+            uint32_t valid = 0xFFFFu;
+            if (len == TILE) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int e0 = 4 * (warp * 128 + lane + 32 * q);
-                col[q] = (int32_t)(a + e0);
-                if (e0 + 4 <= bulk_n) {
-                    const float4 f = *reinterpret_cast<const float4*>(st + e0);
+                for (int q = 0; q < 4; ++q) {
+                    const float4 f = *reinterpret_cast<const float4*>(st + 4 * (warp * 128 + lane + 32 * q));
                     vv[4 * q] = f.x; vv[4 * q + 1] = f.y; vv[4 * q + 2] = f.z; vv[4 * q + 3] = f.w;
-                    valid |= 0xFu << (4 * q);
-                } else {
+                }
+            } else {
+                valid = 0;
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) {
-                        const int e = e0 + c4;
-                        vv[4 * q + c4] = 0.f;
-                        if (e < len) {
-                            vv[4 * q + c4] = (e < bulk_n) ? st[e] : xr[a + e];
-                            valid |= 1u << (4 * q + c4);
-                        }
+                for (int b = 0; b < 16; ++b) {
+                    const int e = 4 * (warp * 128 + lane + 32 * (b >> 2)) + (b & 3);
+                    vv[b] = -INFINITY;
+                    if (e < len) {
+                        vv[b] = (e < bulk_n) ? st[e] : xr[a + e];
+                        valid |= 1u << b;
                     }
                 }
             }
-            // the stage's bytes are in registers: hand it back to the producer
-            __syncwarp();
-            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.ebar[s])) : "memory");
+            // Screen the 16 with one max.NaN reduction (missing slots hold -inf).
+            float mx8[8];
+#pragma unroll
+            for (int b = 0; b < 8; ++b) mx8[b] = fmax_nan(vv[2 * b], vv[2 * b + 1]);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) mx8[b] = fmax_nan(mx8[2 * b], mx8[2 * b + 1]);
+            const float mxn = fmax_nan(fmax_nan(mx8[0], mx8[1]), fmax_nan(mx8[2], mx8[3]));
+            nan |= (mxn != mxn);
             if (t == 0) {
                 // Seed: the k-th largest of the 256 per-lane maxima of the
                 // unit's first tile (k <= KWS distinct logits are >= it).
                 float mx = -INFINITY;
 #pragma unroll
-                for (int b = 0; b < 16; ++b)
-                    if ((valid >> b) & 1u) mx = vv[b] > mx ? vv[b] : mx;
+                for (int b = 0; b < 16; ++b) mx = vv[b] > mx ? vv[b] : mx;
                 ckey[tid] = fkey(mx);
                 csync();
                 const uint32_t kth = block_select_kth(ckey, NT, k, sm);
                 if (tid == 0) sm.thr_key = kth;
                 csync();
             }
-            if (!stopped) {
-                const uint32_t tk = *reinterpret_cast<volatile uint32_t*>(&sm.thr_key);
-                float thr = fkey_inv(tk);
-                thr = thr > wthr ? thr : wthr;
-                uint32_t m = 0;
+            float thr = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&sm.thr_key));
+            thr = thr > wthr ? thr : wthr;
+            if (!stopped && __any_sync(0xffffffffu, mxn >= thr)) {
+                auto pass_bits = [&](float th) -> uint32_t {
+                    uint32_t m = 0;
+                    if (mxn >= th) {
 #pragma unroll
-                for (int b = 0; b < 16; ++b) {
-                    nan |= (((valid >> b) & 1u) && vv[b] != vv[b]);
-                    if (((valid >> b) & 1u) && vv[b] >= thr) m |= 1u << b;
-                }
-                if (!warp_append(wk, wi, wcnt, m, vv, col)) {
-                    // does not fit: raise the bound, filter again, and give up
-                    // (massive ties: the exact replay takes the row) if it still does not fit
+                        for (int b = 0; b < 16; ++b)
+                            if (vv[b] >= th) m |= 1u << b;
+                    }
+                    return m & valid;
+                };
+                uint32_t m = pass_bits(thr);
+                int c = __popc(m);
+                int incl = warp_incl_scan(c);
+                int tot = __shfl_sync(0xffffffffu, incl, 31);
+                if (wcnt + tot > WCAP) {
+                    // does not fit: raise the bound and filter again; if it still
+                    // does not fit (massive ties) the exact replay takes the row
                     warp_shrink(wk, wi, wcnt, wthr, k, whist, sm);
-                    const uint32_t tk2 = *reinterpret_cast<volatile uint32_t*>(&sm.thr_key);
-                    float thr2 = fkey_inv(tk2);
+                    float thr2 = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&sm.thr_key));
                     thr2 = thr2 > wthr ? thr2 : wthr;
-                    m = 0;
-#pragma unroll
-                    for (int b = 0; b < 16; ++b)
-                        if (((valid >> b) & 1u) && vv[b] >= thr2) m |= 1u << b;
-                    if (!warp_append(wk, wi, wcnt, m, vv, col)) {
+                    m = pass_bits(thr2);
+                    c = __popc(m);
+                    incl = warp_incl_scan(c);
+                    tot = __shfl_sync(0xffffffffu, incl, 31);
+                    if (wcnt + tot > WCAP) {
                         stopped = true;
+                        m = 0;
+                        tot = 0;
                         if (lane == 0) atomicOr(&sm.flags, FLAG_OVERFLOW);
                     }
                 }
-                if (wcnt > WTRIG) {
+                // append the passing logits, reading them back from the stage
+                int pos = wcnt + incl - c;
+                while (m) {
+                    const int b = __ffs(m) - 1;
+                    m &= m - 1;
+                    const int e = 4 * (warp * 128 + lane + 32 * (b >> 2)) + (b & 3);
+                    const float v = (e < bulk_n) ? st[e] : xr[a + e];
+                    wk[pos] = fkey(v);
+                    wi[pos] = (int32_t)(a + e);
+                    ++pos;
+                }
+                wcnt += tot;
+                if (wcnt > wtrig) {
                     MXS_PROF_T0(ts);
                     warp_shrink(wk, wi, wcnt, wthr, k, whist, sm);
                     MXS_PROF_ADD(2, ts);
                 }
-            } else {
-#pragma unroll
-                for (int b = 0; b < 16; ++b) nan |= (((valid >> b) & 1u) && vv[b] != vv[b]);
             }
+            // every lane of the warp is done with the stage: hand it back
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.ebar[s])) : "memory");
             MXS_PROF_ADD(1, tc);
         }
         // Gather the warp buffers (entries >= the final bound) into ckey/cidx[0, cnt).
