@@ -501,14 +501,34 @@ extern "C" __attribute__((visibility("default"))) int mxs_prof_read(unsigned lon
 // the highest bound published.
 // ---------------------------------------------------------------------------
 
-// Raise the warp's bound to the k-th largest key it holds and drop the rest.
-__device__ __forceinline__ void warp_shrink(uint32_t* wk, int32_t* wi, int& wcnt, float& wthr, int k,
-                                            uint32_t* hist, Misc& sm) {
-    if (wcnt < k) return;
-    const uint32_t kth = warp_select_kth(wk, wcnt, k, hist);
-    wcnt = warp_compact_ge(wk, wi, wcnt, kth);
-    wthr = fkey_inv(kth);
-    if ((threadIdx.x & 31) == 0) atomicMax(&sm.thr_key, kth);
+// Tighten the shared bound and compact the warp's buffer to it. The warp
+// publishes the m-th largest key it holds (m = ceil(k / NWARPS)); the consumer
+// warps filter disjoint slices of the unit, so at least NWARPS * m >= k logits
+// are >= the smallest value published by all of them, which is therefore a
+// valid bound, close to the unit's k-th largest. Until every warp has published,
+// a warp holding k or more entries offers its own k-th largest instead.
+__device__ __forceinline__ void warp_shrink(uint32_t* wk, int32_t* wi, int& wcnt, int k, uint32_t* hist, Misc& sm) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int m = (k + NWARPS - 1) / NWARPS;
+    if (wcnt >= m) {
+        const uint32_t km = warp_select_kth(wk, wcnt, m, hist);
+        if (lane == 0) atomicMax(&sm.pub[warp], km);
+    }
+    __syncwarp();
+    uint32_t mn = (lane < NWARPS) ? *reinterpret_cast<volatile uint32_t*>(&sm.pub[lane]) : 0xFFFFFFFFu;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, d));
+    if (mn == 0u) {
+        if (wcnt >= k) {
+            const uint32_t kk = warp_select_kth(wk, wcnt, k, hist);
+            if (lane == 0) atomicMax(&sm.thr_key, kk);
+        }
+    } else if (lane == 0) {
+        atomicMax(&sm.thr_key, mn);
+    }
+    __syncwarp();
+    const uint32_t T = *reinterpret_cast<volatile uint32_t*>(&sm.thr_key);
+    wcnt = warp_compact_ge(wk, wi, wcnt, T);
 }
 
 __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
@@ -577,9 +597,8 @@ __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
     uint32_t* wk = ckey + warp * WCAP;
     int32_t* wi = cidx + warp * WCAP;
     uint32_t* whist = whist_all + warp * 256;
-    // shrink a warp buffer once it holds 2k entries (at least 64): the bound
-    // then rises every ~k appended logits
-    const int wtrig = min(WTRIG, max(2 * k, 64));
+    // shrink a warp buffer once it holds 2m entries (at least 32), m = ceil(k / NWARPS)
+    const int wtrig = min(WTRIG, max(2 * ((k + NWARPS - 1) / NWARPS), 32));
     uint32_t cseq = 0;
     MXS_PROF_T0(ttot);
     for (int64_t j = 0; j < nj; ++j) {
@@ -593,12 +612,12 @@ __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
             sm.cnt = 0;
             sm.thr = -INFINITY;
             sm.thr_key = 0u;  // below every key of a non-NaN logit
+            for (int w = 0; w < NWARPS; ++w) sm.pub[w] = 0u;
             atomicAnd(&sm.flags, FLAG_TIMEOUT);  // a producer timeout stays; row flags start clear
         }
         csync();
-        int wcnt = 0, nan = 0;
+        int wcnt = 0, nan = 0, ntrig = wtrig;
         bool stopped = false;
-        float wthr = -INFINITY;
         for (int t = 0; t < nt; ++t, ++cseq) {
             const int64_t a = ((int64_t)c * TPC + t) * TILE;
             const int len = (int)(min(a + TILE, V) - a);
@@ -650,8 +669,7 @@ __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
                 if (tid == 0) sm.thr_key = kth;
                 csync();
             }
-            float thr = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&sm.thr_key));
-            thr = thr > wthr ? thr : wthr;
+            const float thr = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&sm.thr_key));
             if (!stopped && __any_sync(0xffffffffu, mxn >= thr)) {
                 auto pass_bits = [&](float th) -> uint32_t {
                     uint32_t m = 0;
@@ -669,9 +687,8 @@ __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
                 if (wcnt + tot > WCAP) {
                     // does not fit: raise the bound and filter again; if it still
                     // does not fit (massive ties) the exact replay takes the row
-                    warp_shrink(wk, wi, wcnt, wthr, k, whist, sm);
-                    float thr2 = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&sm.thr_key));
-                    thr2 = thr2 > wthr ? thr2 : wthr;
+                    warp_shrink(wk, wi, wcnt, k, whist, sm);
+                    const float thr2 = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&sm.thr_key));
                     m = pass_bits(thr2);
                     c = __popc(m);
                     incl = warp_incl_scan(c);
@@ -695,9 +712,12 @@ __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
                     ++pos;
                 }
                 wcnt += tot;
-                if (wcnt > wtrig) {
+                if (wcnt > ntrig) {
                     MXS_PROF_T0(ts);
-                    warp_shrink(wk, wi, wcnt, wthr, k, whist, sm);
+                    warp_shrink(wk, wi, wcnt, k, whist, sm);
+                    // hysteresis: if the bound has not caught up yet, let the
+                    // buffer grow before selecting again
+                    ntrig = min(WCAP - 64, max(wtrig, 2 * wcnt));
                     MXS_PROF_ADD(2, ts);
                 }
             }

@@ -84,6 +84,7 @@ struct Misc {
     uint64_t bar[STAGES];   // stage full (bytes landed)
     uint64_t ebar[STAGES];  // stage empty (every consumer warp is done with it)
     uint32_t thr_key;       // running threshold key shared by the consumer warps
+    uint32_t pub[NWARPS];   // per consumer warp: the m-th largest key it has held (m = ceil(k / NWARPS))
     uint32_t hist[256];
     int warp_tot[NWARPS];
     uint32_t warp_or[NWARPS];
