@@ -135,6 +135,26 @@ MXS_API int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count
                      double top_p, double min_p, const double* d_u, int32_t* d_next, int32_t* d_topk_idx,
                      double* d_topk_prob, uint32_t* d_row_flags, void* stream);
 
+/*
+ * No counterpart in the reference: an addition of this library for callers that
+ * cannot allocate device memory (hosts whose memory pool owns the whole GPU, or
+ * that forbid allocation on the per-token path). Same arguments and results as
+ * mxs_sample_topk_ex without a workspace: the scratch is a fixed array of
+ * MXS_NOALLOC_SCRATCH_BYTES compiled into the library, held by every GPU that
+ * loads it until the process exits; no call allocates or frees memory.
+ * Returns MXS_ERR_WORKSPACE when the shape needs more scratch than that
+ * (mxs_workspace_size tells how much; large top_k, above ~3000, needs the most).
+ * The first call on a device looks up the array's device address; make that
+ * call before any stream capture. All calls share the one array, so calls
+ * that overlap on the GPU (other streams, other threads) race and must be
+ * serialised by the caller.
+ */
+#define MXS_NOALLOC_SCRATCH_BYTES (16u << 20)
+MXS_API int mxs_sample_topk_noalloc(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld,
+                                    double temperature, int top_k, double top_p, double min_p, const double* d_u,
+                                    int32_t* d_next, int32_t* d_topk_idx, double* d_topk_prob,
+                                    uint32_t* d_row_flags, void* stream);
+
 /* OR of MXS_ROW_* flags of every row that hit MXS_ROW_TIMEOUT since the last clear
  * on the current device (synchronises the device). */
 MXS_API int mxs_get_status(uint32_t* flags, int clear);

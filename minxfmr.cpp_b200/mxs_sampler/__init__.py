@@ -36,7 +36,7 @@ ROW_TIMEOUT = 8
 EXPORTS = (
     "mxs_sample_topk", "mxs_sample_topk_ex", "mxs_workspace_size", "mxs_workspace_init",
     "mxs_sample_topk_host", "mxs_shard_candidates", "mxs_merge_sample", "mxs_get_status",
-    "mxs_version",
+    "mxs_version", "mxs_sample_topk_noalloc",
 )
 
 _P = ctypes.c_void_p
@@ -54,6 +54,7 @@ _SIGS = {
     "mxs_shard_candidates": [_P, _I64, _I64, _I64, _I64, _I, _I, _P, _P, _P, _P],
     "mxs_merge_sample": [_P, _P, _P, _I, _I, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _P],
     "mxs_get_status": [ctypes.POINTER(ctypes.c_uint32), _I],
+    "mxs_sample_topk_noalloc": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _P],
 }
 
 _lib = None
@@ -147,6 +148,31 @@ def sample(logits, temperature, top_k, u, top_p=1.0, min_p=0.0, out=None, return
     _check("mxs_sample_topk_ex", rc)
     if return_flags:
         return nxt, idx, prob, flags
+    return nxt, idx, prob
+
+
+def sample_noalloc(logits, temperature, top_k, u, top_p=1.0, min_p=0.0, out=None, stream=None):
+    """As sample(), through mxs_sample_topk_noalloc: for hosts that cannot let
+    the library allocate device memory (their pool owns the GPU, or the
+    per-token path forbids allocation). Scratch comes from a fixed array in the
+    library; the caller still owns the outputs (pass them in `out` to avoid any
+    allocation here: (next, topk_idx, topk_prob, row_flags), any of the last
+    three may be None). Calls that overlap on the GPU share that array and race."""
+    _need_cuda(logits, "logits", torch.float32)
+    _need_cuda(u, "u", torch.float64)
+    rows, vocab = logits.shape
+    k = k_use(int(top_k), vocab)
+    if out is None:
+        dev = logits.device
+        out = (torch.empty(rows, dtype=torch.int32, device=dev),
+               torch.empty((rows, k), dtype=torch.int32, device=dev),
+               torch.empty((rows, k), dtype=torch.float64, device=dev), None)
+    nxt, idx, prob, flags = out
+    with torch.cuda.device(logits.device):
+        rc = load().mxs_sample_topk_noalloc(_ptr(logits), rows, vocab, logits.stride(0), float(temperature),
+                                            int(top_k), float(top_p), float(min_p), _ptr(u), _ptr(nxt), _ptr(idx),
+                                            _ptr(prob), _ptr(flags), _stream(stream))
+    _check("mxs_sample_topk_noalloc", rc)
     return nxt, idx, prob
 
 
