@@ -111,15 +111,28 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 #ifdef MXS_PROFILE
 constexpr int PROF_CTAS = 1024, PROF_PHASES = 8;
 __device__ unsigned long long g_mxs_prof[PROF_CTAS][PROF_PHASES];
+__shared__ unsigned long long s_mxs_prof[PROF_PHASES];  // per CTA, flushed once at kernel end
 #define MXS_PROF_T0(v) long long v = (threadIdx.x == 0) ? clock64() : 0
-#define MXS_PROF_ADD(ph, v)                                                             \
-    do {                                                                                \
-        if (threadIdx.x == 0 && blockIdx.x < mxs::PROF_CTAS)                            \
-            mxs::g_mxs_prof[blockIdx.x][ph] += (unsigned long long)(clock64() - (v));   \
+#define MXS_PROF_ADD(ph, v)                                                          \
+    do {                                                                             \
+        if (threadIdx.x == 0) mxs::s_mxs_prof[ph] += (unsigned long long)(clock64() - (v)); \
+    } while (0)
+#define MXS_PROF_BEGIN()                                                             \
+    do {                                                                             \
+        if (threadIdx.x == 0)                                                        \
+            for (int i_ = 0; i_ < mxs::PROF_PHASES; ++i_) mxs::s_mxs_prof[i_] = 0;   \
+    } while (0)
+#define MXS_PROF_FLUSH()                                                             \
+    do {                                                                             \
+        if (threadIdx.x == 0 && blockIdx.x < mxs::PROF_CTAS)                         \
+            for (int i_ = 0; i_ < mxs::PROF_PHASES; ++i_)                            \
+                mxs::g_mxs_prof[blockIdx.x][i_] += mxs::s_mxs_prof[i_];              \
     } while (0)
 #else
 #define MXS_PROF_T0(v) (void)0
 #define MXS_PROF_ADD(ph, v) (void)0
+#define MXS_PROF_BEGIN() (void)0
+#define MXS_PROF_FLUSH() (void)0
 #endif
 
 // Barrier over the CTA's NT sampling threads only (named barrier 1). A

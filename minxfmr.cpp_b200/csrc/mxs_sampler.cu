@@ -333,6 +333,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
 
     uint32_t cseq = 0;
     const int trig = min(CAP / 2, max(512, 4 * k));
+    MXS_PROF_BEGIN();
     MXS_PROF_T0(ttot);
     for (int64_t j = 0; j < nj; ++j) {
         const int64_t u = blockIdx.x + j * G;
@@ -474,6 +475,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
         MXS_PROF_ADD(3, tf);
     }
     MXS_PROF_ADD(7, ttot);
+    MXS_PROF_FLUSH();
     if (TMA && tid == 0)
         for (int s = 0; s < STAGES; ++s) mbar_inval(&sm.bar[s]);
 }
@@ -600,6 +602,7 @@ __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
     // shrink a warp buffer once it holds 2m entries (at least 32), m = ceil(k / NWARPS)
     const int wtrig = min(WTRIG, max(2 * ((k + NWARPS - 1) / NWARPS), 32));
     uint32_t cseq = 0;
+    MXS_PROF_BEGIN();
     MXS_PROF_T0(ttot);
     for (int64_t j = 0; j < nj; ++j) {
         const int64_t u = blockIdx.x + j * G;
@@ -765,6 +768,7 @@ __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
         MXS_PROF_ADD(3, tf);
     }
     MXS_PROF_ADD(7, ttot);
+    MXS_PROF_FLUSH();
 }
 
 // ---------------------------------------------------------------------------
