@@ -10,6 +10,7 @@
 
 #include "../../include/mxs_sampler.h"
 #include "mxs_launch.h"
+#include "mxs_stream.h"
 #include "mxs_sampler_kernel.cuh"
 
 namespace {
@@ -50,6 +51,9 @@ int current_device(Device** out) {
         if (prop.major != 10) return MXS_ERR_NO_DEVICE;  // built for sm_100a only
         int bps = 0;
         if (mxs::sample_kernel_configure(&bps) != cudaSuccess || bps < 1) return MXS_ERR_CUDA;
+        int bps2 = 0;
+        if (mxs::stream_path_configure(&bps2) != cudaSuccess || bps2 < 1) return MXS_ERR_CUDA;
+        bps = std::min(bps, bps2);
         d.sms = prop.multiProcessorCount;
         d.blocks_per_sm = bps;
         d.ready = true;
@@ -64,6 +68,8 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 struct Plan {
     int k_use = 1;
     int S = 1, tpc = 1, grid = 1, outcap = 0;
+    bool split = false;  // three-kernel path (stream -> finish -> exact)
+    size_t off_rcand = 0, off_rcnt = 0, off_rflag = 0, off_xcount = 0, off_xrows = 0, zero_bytes = 0;
     int64_t units = 0;
     size_t off_counter = 0, off_state = 0, off_status = 0, off_ccount = 0, off_cand = 0, off_heap = 0,
            off_prob = 0, total = 0;
@@ -75,9 +81,30 @@ int clamp_k(int top_k, int64_t vocab) {
     return (int)k;
 }
 
-Plan make_plan(const Device& d, int64_t rows, int64_t vocab, int k_use, bool merge_mode) {
+// The three-kernel path takes sampling calls with k <= KSPLIT on 16-byte aligned
+// rows. MXS_SAMPLER_PATH selects another kernel for every call ("fused": the
+// one-launch warp-specialised kernel, "block": the CTA-synchronous one); the
+// parity tests run all three. MXS_SAMPLER_BLOCK_PATH=1 is the older spelling of
+// "block".
+int path_override() {
+    const char* bp = getenv("MXS_SAMPLER_BLOCK_PATH");
+    if (bp && bp[0] == '1') return 2;
+    const char* ps = getenv("MXS_SAMPLER_PATH");
+    if (ps && ps[0] == 'f') return 1;
+    if (ps && ps[0] == 'b') return 2;
+    return 0;
+}
+
+bool use_split(int64_t vocab, int64_t ld, const float* logits, int k_use) {
+    const bool tma = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && (ld % 4 == 0);
+    (void)vocab;
+    return tma && k_use <= mxs::KSPLIT && path_override() == 0;
+}
+
+Plan make_plan(const Device& d, int64_t rows, int64_t vocab, int k_use, bool merge_mode, bool split = false) {
     Plan pl;
     pl.k_use = k_use;
+    pl.split = split;
     const int64_t full = (int64_t)d.sms * d.blocks_per_sm;
     const int64_t ntl = (vocab + mxs::TILE - 1) / mxs::TILE;
     if (merge_mode || k_use > mxs::KFAST) {
@@ -94,7 +121,7 @@ Plan make_plan(const Device& d, int64_t rows, int64_t vocab, int k_use, bool mer
         pl.units = rows * pl.S;
         pl.grid = (int)std::max<int64_t>(1, std::min<int64_t>(pl.units, full));
     }
-    pl.outcap = pl.S > 1 ? k_use + 256 : 0;
+    pl.outcap = (pl.S > 1 && !split) ? k_use + 256 : 0;
     size_t o = 0;
     pl.off_status = o;
     o = align_up(o + 256, 256);
@@ -107,7 +134,18 @@ Plan make_plan(const Device& d, int64_t rows, int64_t vocab, int k_use, bool mer
     pl.off_state = o;
     o = align_up(o + sizeof(uint32_t) * (size_t)full, 256);
     pl.off_ccount = o;
-    if (pl.S > 1) {
+    if (split) {
+        // per-row counters, flags and the exact-row count: cleared by every call
+        pl.off_rcnt = o;
+        pl.off_rflag = pl.off_rcnt + sizeof(uint32_t) * (size_t)rows;
+        pl.off_xcount = pl.off_rflag + sizeof(uint32_t) * (size_t)rows;
+        pl.zero_bytes = pl.off_xcount + 16 - pl.off_rcnt;
+        o = align_up(pl.off_xcount + 16, 256);
+        pl.off_xrows = o;
+        o = align_up(o + sizeof(int32_t) * (size_t)rows, 256);
+        pl.off_rcand = o;
+        o = align_up(o + sizeof(uint64_t) * (size_t)rows * mxs::SPLIT_ROW_CAP, 256);
+    } else if (pl.S > 1) {
         o = align_up(o + sizeof(uint32_t) * (size_t)rows * pl.S, 256);
         pl.off_cand = o;
         o = align_up(o + sizeof(uint64_t) * (size_t)rows * pl.S * pl.outcap, 256);
@@ -147,6 +185,14 @@ void fill_workspace(Params& p, const Plan& pl, void* ws) {
     p.chunk_cand = pl.S > 1 ? reinterpret_cast<uint64_t*>(b + pl.off_cand) : nullptr;
     p.heap_ws = pl.off_heap ? reinterpret_cast<mxs::Ent*>(b + pl.off_heap) : nullptr;
     p.prob_ws = pl.off_prob ? reinterpret_cast<double*>(b + pl.off_prob) : nullptr;
+    if (pl.split) {
+        p.row_cand = reinterpret_cast<uint64_t*>(b + pl.off_rcand);
+        p.row_cnt = reinterpret_cast<uint32_t*>(b + pl.off_rcnt);
+        p.row_flag = reinterpret_cast<uint32_t*>(b + pl.off_rflag);
+        p.row_cap = mxs::SPLIT_ROW_CAP;
+        p.xcount = reinterpret_cast<uint32_t*>(b + pl.off_xcount);
+        p.xrows = reinterpret_cast<int32_t*>(b + pl.off_xrows);
+    }
 }
 
 void clamp_p(double* top_p, double* min_p) {  // src/api/minxfmr.cpp:2109-2111
@@ -155,16 +201,20 @@ void clamp_p(double* top_p, double* min_p) {  // src/api/minxfmr.cpp:2109-2111
     if (*min_p > 1.0) *min_p = 1.0;
 }
 
-int launch(Params& p, const Plan& pl, cudaStream_t stream) {
+int launch(Params& p, const Plan& pl, cudaStream_t stream, int sms = 148) {
     p.S = pl.S;
     p.tiles_per_chunk = pl.tpc;
     p.units = pl.units;
     p.outcap = pl.outcap;
+    if (pl.split) {
+        if (cudaMemsetAsync(p.row_cnt, 0, pl.zero_bytes, stream) != cudaSuccess) return MXS_ERR_CUDA;
+        if (mxs::stream_path_launch(p, pl.grid, sms, stream) != cudaSuccess) return MXS_ERR_CUDA;
+        return MXS_OK;
+    }
     const bool tma = (reinterpret_cast<uintptr_t>(p.logits) % 16 == 0) && (p.ld % 4 == 0);
     // MXS_SAMPLER_BLOCK_PATH=1 selects the CTA-synchronous streaming kernel for
     // every k (the parity tests run both kernels).
-    const char* bp = getenv("MXS_SAMPLER_BLOCK_PATH");
-    p.force_block_path = (bp && bp[0] == '1') ? 1 : 0;
+    p.force_block_path = path_override() == 2 ? 1 : 0;
     if (mxs::sample_kernel_launch(p, pl.grid, tma, stream) != cudaSuccess) return MXS_ERR_CUDA;
     return MXS_OK;
 }
@@ -185,7 +235,10 @@ int mxs_workspace_size(int64_t rows, int64_t vocab, int top_k, size_t* bytes) {
     Device* d;
     int rc = current_device(&d);
     if (rc) return rc;
-    *bytes = make_plan(*d, rows, vocab, clamp_k(top_k, vocab), false).total;
+    const int k_use = clamp_k(top_k, vocab);
+    size_t need = make_plan(*d, rows, vocab, k_use, false).total;
+    if (k_use <= mxs::KSPLIT) need = std::max(need, make_plan(*d, rows, vocab, k_use, false, true).total);
+    *bytes = need;
     return MXS_OK;
 }
 
@@ -207,7 +260,8 @@ int mxs_sample_topk_ex(const float* d_logits, int64_t rows, int64_t vocab, int64
     int rc = current_device(&d);
     if (rc) return rc;
     clamp_p(&top_p, &min_p);
-    const Plan pl = make_plan(*d, rows, vocab, clamp_k(top_k, vocab), false);
+    const int k_use = clamp_k(top_k, vocab);
+    const Plan pl = make_plan(*d, rows, vocab, k_use, false, use_split(vocab, ld, d_logits, k_use));
     void* ws = d_workspace;
     if (!ws) {
         rc = ensure_library_ws(*d, pl.total, (cudaStream_t)stream);
@@ -232,7 +286,7 @@ int mxs_sample_topk_ex(const float* d_logits, int64_t rows, int64_t vocab, int64
     p.row_flags = d_row_flags;
     p.mode = mxs::MODE_SAMPLE;
     fill_workspace(p, pl, ws);
-    return launch(p, pl, (cudaStream_t)stream);
+    return launch(p, pl, (cudaStream_t)stream, d->sms);
 }
 
 int mxs_sample_topk(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,

@@ -38,6 +38,64 @@ __device__ __forceinline__ double seq_sum(const double* p, int n) {
     return s;
 }
 
+// Top-p then min-p on the normalised probabilities pbuf[0, k), renormalising
+// in place as src/api/minxfmr.cpp:2128-2165 does; returns how many stay. Serial.
+__device__ inline int truncate_p(double* pbuf, int k, double top_p, double min_p) {
+    int n = k;
+    if (top_p < 1.0) {  // src/api/minxfmr.cpp:2128-2145
+        double cum = 0.0;
+        n = 0;
+        for (int i = 0; i < k; ++i) {
+            cum += pbuf[i];
+            n = i + 1;
+            if (cum >= top_p) break;
+        }
+        if (n < 1) n = 1;
+        double renorm = 0.0;
+        for (int i = 0; i < n; ++i) renorm += pbuf[i];
+        if (renorm > 0.0)
+            for (int i = 0; i < n; ++i) pbuf[i] /= renorm;
+    }
+    if (min_p > 0.0 && n > 1) {  // src/api/minxfmr.cpp:2147-2165
+        const double thr = pbuf[0] * min_p;
+        int keep = 1;
+        for (int i = 1; i < n; ++i) {
+            if (pbuf[i] >= thr) keep = i + 1;
+            else break;
+        }
+        n = keep;
+        double renorm = 0.0;
+        for (int i = 0; i < n; ++i) renorm += pbuf[i];
+        if (renorm > 0.0)
+            for (int i = 0; i < n; ++i) pbuf[i] /= renorm;
+    }
+    return n;
+}
+
+// Running partial sums of pbuf[0, n) in place, last forced to 1.0, then the
+// first index whose cumulative value is not below u (discrete_distribution's
+// _M_initialize + operator(), bits/random.tcc:2657-2714). Serial.
+__device__ inline int cdf_pick(double* pbuf, int n, double u) {
+    double run = 0.0;
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {  // loads of a block of 8 issue together; the adds stay in order
+        double v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = pbuf[i + j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            run += v[j];
+            pbuf[i + j] = run;
+        }
+    }
+    for (; i < n; ++i) {
+        run += pbuf[i];
+        pbuf[i] = run;
+    }
+    pbuf[n - 1] = 1.0;
+    return lower_bound_cp(pbuf, n, u);
+}
+
 // e[0, k): the row's top-k in the reference's order. pbuf: k doubles.
 // Follows src/api/minxfmr.cpp:2104-2169 and libstdc++'s discrete_distribution
 // (bits/random.tcc:2657-2714): each double operation of the reference happens
@@ -73,34 +131,7 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
     }
     csync();
     if (tid == 0) {
-        int n = k;
-        if (p.top_p < 1.0) {  // src/api/minxfmr.cpp:2128-2145
-            double cum = 0.0;
-            n = 0;
-            for (int i = 0; i < k; ++i) {
-                cum += pbuf[i];
-                n = i + 1;
-                if (cum >= p.top_p) break;
-            }
-            if (n < 1) n = 1;
-            double renorm = 0.0;
-            for (int i = 0; i < n; ++i) renorm += pbuf[i];
-            if (renorm > 0.0)
-                for (int i = 0; i < n; ++i) pbuf[i] /= renorm;
-        }
-        if (p.min_p > 0.0 && n > 1) {  // src/api/minxfmr.cpp:2147-2165
-            const double thr = pbuf[0] * p.min_p;
-            int keep = 1;
-            for (int i = 1; i < n; ++i) {
-                if (pbuf[i] >= thr) keep = i + 1;
-                else break;
-            }
-            n = keep;
-            double renorm = 0.0;
-            for (int i = 0; i < n; ++i) renorm += pbuf[i];
-            if (renorm > 0.0)
-                for (int i = 0; i < n; ++i) pbuf[i] /= renorm;
-        }
+        const int n = truncate_p(pbuf, k, p.top_p, p.min_p);
         sm.krem = n;
         sm.sum = (n >= 2) ? seq_sum(pbuf, n) : 0.0;
     }
@@ -114,26 +145,7 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
     const double s2 = sm.sum;
     for (int i = tid; i < n; i += NT) pbuf[i] = pbuf[i] / s2;
     csync();
-    if (tid == 0) {
-        double run = 0.0;
-        int i = 0;
-        for (; i + 8 <= n; i += 8) {  // loads of a block of 8 issue together; the adds stay in order
-            double v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = pbuf[i + j];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                run += v[j];
-                pbuf[i + j] = run;
-            }
-        }
-        for (; i < n; ++i) {
-            run += pbuf[i];
-            pbuf[i] = run;
-        }
-        pbuf[n - 1] = 1.0;
-        p.next[row] = e[lower_bound_cp(pbuf, n, p.u[row])].i;
-    }
+    if (tid == 0) p.next[row] = e[cdf_pick(pbuf, n, p.u[row])].i;
     csync();
 }
 

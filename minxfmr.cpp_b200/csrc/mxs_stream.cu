@@ -1,0 +1,450 @@
+// Three-kernel sampling path for k <= KSPLIT on 16-byte aligned rows.
+//
+//  1. stream_select_kernel: a producer warp streams every tile of the CTA's
+//     (row, chunk) units through a bulk-copy ring; 8 consumer warps each filter
+//     a 512-logit slice of every tile against a shared lower bound of the
+//     unit's k-th largest value, with no CTA-wide barrier at all: per-unit
+//     state lives in an 8-slot ring recycled by the last warp to leave a unit,
+//     and each warp appends its surviving candidates to the row's list in
+//     global memory when it leaves the unit.
+//  2. finish_rows_kernel: one warp per row selects the k-th largest candidate,
+//     sorts the k survivors in registers, checks for ties and draws.
+//  3. exact_rows_kernel: one CTA per row the finish kernel handed over (a tie,
+//     a NaN, an overflow) replays the reference's heap process over the row.
+#include <cmath>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "mxs_rowfinish.cuh"
+#include "mxs_stream.h"
+
+namespace mxs {
+
+constexpr int KSPLIT_K = 64;        // largest k of this path (register sort of 64)
+constexpr int SW_CAP = 256;         // candidates per consumer warp
+constexpr int SLOTS = 8;            // per-unit state ring (> the STAGES a warp can run ahead)
+constexpr int FCAP = 1024;          // candidates per row the finish warp takes
+static_assert(KSPLIT_K == KSPLIT, "KSPLIT must match the register sort");
+static_assert(FCAP == SPLIT_ROW_CAP, "a finish warp takes a whole row list");
+
+struct UnitState {
+    uint32_t thr_key;        // shared bound (order-preserving key), only grows
+    uint32_t pub[NWARPS];    // per warp: m-th largest key it has held, m = ceil(k / NWARPS)
+    uint32_t done;           // warps that have left the unit
+};
+
+struct StreamSmem {
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    UnitState us[SLOTS];
+};
+
+constexpr size_t S_RING = size_t(STAGES) * TILE * 4;
+constexpr size_t S_WBUF = size_t(NWARPS) * SW_CAP * 8;
+constexpr size_t S_HIST = size_t(NWARPS) * 256 * 4;
+constexpr size_t S_SMEM = S_RING + S_WBUF + S_HIST + sizeof(StreamSmem);
+
+// Publish this warp's m-th largest key; the smallest value every warp has
+// published bounds the unit's k-th largest from below (the warps' slices are
+// disjoint and NWARPS * m >= k). Until all have published, a warp holding k
+// or more entries offers its own k-th largest. Then compact to the bound.
+__device__ __forceinline__ void stream_shrink(uint32_t* wk, int32_t* wi, int& wcnt, int k, uint32_t* hist,
+                                              UnitState& us) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int m = (k + NWARPS - 1) / NWARPS;
+    if (wcnt >= m) {
+        const uint32_t km = warp_select_kth(wk, wcnt, m, hist);
+        if (lane == 0) atomicMax(&us.pub[warp], km);
+    }
+    __syncwarp();
+    uint32_t mn = (lane < NWARPS) ? *reinterpret_cast<volatile uint32_t*>(&us.pub[lane]) : 0xFFFFFFFFu;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, d));
+    if (mn == 0u) {
+        if (wcnt >= k) {
+            const uint32_t kk = warp_select_kth(wk, wcnt, k, hist);
+            if (lane == 0) atomicMax(&us.thr_key, kk);
+        }
+    } else if (lane == 0) {
+        atomicMax(&us.thr_key, mn);
+    }
+    __syncwarp();
+    wcnt = warp_compact_ge(wk, wi, wcnt, *reinterpret_cast<volatile uint32_t*>(&us.thr_key));
+}
+
+// Warp-wide bitonic sort of one key per lane, descending.
+__device__ __forceinline__ uint32_t warp_sort32_desc(uint32_t v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const uint32_t o = __shfl_xor_sync(0xffffffffu, v, stride);
+            const bool desc = ((lane & size) == 0) || size == 32;
+            const bool keep_max = (desc == ((lane & stride) == 0));
+            v = keep_max ? max(v, o) : min(v, o);
+        }
+    }
+    return v;
+}
+
+__global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    float* ring = reinterpret_cast<float*>(smem);
+    uint32_t* wkeys = reinterpret_cast<uint32_t*>(smem + S_RING);
+    int32_t* widx = reinterpret_cast<int32_t*>(smem + S_RING + S_WBUF / 2);
+    uint32_t* whist_all = reinterpret_cast<uint32_t*>(smem + S_RING + S_WBUF);
+    StreamSmem& sm = *reinterpret_cast<StreamSmem*>(smem + S_RING + S_WBUF + S_HIST);
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int k = p.k_use;
+    const int64_t V = p.vocab;
+    const int64_t G = gridDim.x;
+    const int64_t nj = (p.units > (int64_t)blockIdx.x) ? (p.units - blockIdx.x + G - 1) / G : 0;
+    const int S = p.S, TPC = p.tiles_per_chunk;
+    const int64_t NTL = (V + TILE - 1) / TILE;
+    auto unit_tiles = [&](int64_t u) -> int {
+        const int64_t t0 = (int64_t)(u % S) * TPC;
+        return (int)min((int64_t)TPC, NTL - t0);
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], NWARPS);
+        }
+        for (int i = 0; i < SLOTS; ++i) {
+            sm.us[i].thr_key = 0u;
+            sm.us[i].done = 0u;
+            for (int w = 0; w < NWARPS; ++w) sm.us[i].pub[w] = 0u;
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == NWARPS) {  // producer
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            uint32_t seq = 0;
+            for (int64_t j = 0; j < nj; ++j) {
+                const int64_t u = blockIdx.x + j * G;
+                const int64_t row = u / S;
+                const int nt = unit_tiles(u);
+                for (int t = 0; t < nt; ++t, ++seq) {
+                    const int s = seq % STAGES;
+                    if (seq >= STAGES && !mbar_wait_bounded(&sm.empty[s], ((seq / STAGES) - 1) & 1)) {
+                        atomicOr(&p.row_flag[row], FLAG_TIMEOUT);
+                        return;  // consumers time out on the stages that never come
+                    }
+                    const int64_t a = ((int64_t)(u % S) * TPC + t) * TILE;
+                    const int64_t b = min(a + TILE, V);
+                    const uint32_t bytes = (uint32_t)(((b - a) & ~int64_t(3)) * 4);
+                    if (bytes) {
+                        mbar_arrive_expect_tx(&sm.full[s], bytes);
+                        bulk_g2s(ring + s * TILE, p.logits + row * p.ld + a, bytes, &sm.full[s], pol);
+                    } else {
+                        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.full[s])) : "memory");
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    uint32_t* wk = wkeys + warp * SW_CAP;
+    int32_t* wi = widx + warp * SW_CAP;
+    uint32_t* whist = whist_all + warp * 256;
+    const int m = (k + NWARPS - 1) / NWARPS;
+    const int wtrig = max(2 * m, 32);
+    uint32_t cseq = 0;
+    bool dead = false;  // a wait ran out: stop waiting, flag every later row
+    for (int64_t j = 0; j < nj; ++j) {
+        const int64_t u = blockIdx.x + j * G;
+        const int64_t row = u / S;
+        const int c = (int)(u % S);
+        const int nt = unit_tiles(u);
+        const float* xr = p.logits + row * p.ld;
+        UnitState& us = sm.us[j % SLOTS];
+        int wcnt = 0, nan = 0, ntrig = wtrig;
+        uint32_t fl = dead ? FLAG_TIMEOUT : 0u;
+        bool stopped = false;
+        for (int t = 0; t < nt; ++t, ++cseq) {
+            const int64_t a = ((int64_t)c * TPC + t) * TILE;
+            const int len = (int)(min(a + TILE, V) - a);
+            const int bulk_n = len & ~3;
+            const int s = cseq % STAGES;
+            if (!dead && !mbar_wait_bounded(&sm.full[s], (cseq / STAGES) & 1)) {
+                fl |= FLAG_TIMEOUT;
+                dead = true;
+            }
+            const float* st = ring + s * TILE;
+            float vv[16];
+            uint32_t valid = 0xFFFFu;
+            if (len == TILE) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 f = *reinterpret_cast<const float4*>(st + 4 * (warp * 128 + lane + 32 * q));
+                    vv[4 * q] = f.x; vv[4 * q + 1] = f.y; vv[4 * q + 2] = f.z; vv[4 * q + 3] = f.w;
+                }
+            } else {
+                valid = 0;
+#pragma unroll
+                for (int b = 0; b < 16; ++b) {
+                    const int e = 4 * (warp * 128 + lane + 32 * (b >> 2)) + (b & 3);
+                    vv[b] = -INFINITY;
+                    if (e < len) {
+                        vv[b] = (e < bulk_n) ? st[e] : xr[a + e];
+                        valid |= 1u << b;
+                    }
+                }
+            }
+            float mx8[8];
+#pragma unroll
+            for (int b = 0; b < 8; ++b) mx8[b] = fmax_nan(vv[2 * b], vv[2 * b + 1]);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) mx8[b] = fmax_nan(mx8[2 * b], mx8[2 * b + 1]);
+            const float mxn = fmax_nan(fmax_nan(mx8[0], mx8[1]), fmax_nan(mx8[2], mx8[3]));
+            nan |= (mxn != mxn);
+            if (t == 0) {
+                // Seed: this warp's m-th largest lane maximum (m distinct logits
+                // of the slice are >= it); lanes without logits offer nothing.
+                float mx = -INFINITY;
+#pragma unroll
+                for (int b = 0; b < 16; ++b) mx = vv[b] > mx ? vv[b] : mx;
+                const uint32_t key = valid ? fkey(mx) : 0u;
+                const uint32_t sorted = warp_sort32_desc(key);
+                const uint32_t km = __shfl_sync(0xffffffffu, sorted, m - 1);
+                if (lane == 0 && km) atomicMax(&us.pub[warp], km);
+                __syncwarp();
+                uint32_t mn = (lane < NWARPS) ? *reinterpret_cast<volatile uint32_t*>(&us.pub[lane]) : 0xFFFFFFFFu;
+#pragma unroll
+                for (int d = 16; d > 0; d >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, d));
+                if (lane == 0 && mn) atomicMax(&us.thr_key, mn);
+            }
+            const float thr = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
+            if (!stopped && __any_sync(0xffffffffu, mxn >= thr)) {
+                auto pass_bits = [&](float th) -> uint32_t {
+                    uint32_t mm = 0;
+                    if (mxn >= th) {
+#pragma unroll
+                        for (int b = 0; b < 16; ++b)
+                            if (vv[b] >= th) mm |= 1u << b;
+                    }
+                    return mm & valid;
+                };
+                uint32_t mm = pass_bits(thr);
+                int cc = __popc(mm);
+                int incl = warp_incl_scan(cc);
+                int tot = __shfl_sync(0xffffffffu, incl, 31);
+                if (wcnt + tot > SW_CAP) {
+                    stream_shrink(wk, wi, wcnt, k, whist, us);
+                    mm = pass_bits(fkey_inv(*reinterpret_cast<volatile uint32_t*>(&us.thr_key)));
+                    cc = __popc(mm);
+                    incl = warp_incl_scan(cc);
+                    tot = __shfl_sync(0xffffffffu, incl, 31);
+                    if (wcnt + tot > SW_CAP) {  // massive ties: the exact replay takes the row
+                        stopped = true;
+                        fl |= FLAG_OVERFLOW;
+                        mm = 0;
+                        tot = 0;
+                    }
+                }
+                int pos = wcnt + incl - cc;
+                while (mm) {
+                    const int b = __ffs(mm) - 1;
+                    mm &= mm - 1;
+                    const int e = 4 * (warp * 128 + lane + 32 * (b >> 2)) + (b & 3);
+                    const float v = (e < bulk_n) ? st[e] : xr[a + e];
+                    wk[pos] = fkey(v);
+                    wi[pos] = (int32_t)(a + e);
+                    ++pos;
+                }
+                wcnt += tot;
+                if (wcnt > ntrig) {
+                    stream_shrink(wk, wi, wcnt, k, whist, us);
+                    ntrig = min(SW_CAP - 64, max(wtrig, 2 * wcnt));
+                }
+            }
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.empty[s])) : "memory");
+        }
+        // Leave the unit: append the survivors (>= the bound now) to the row's list.
+        const uint32_t T = *reinterpret_cast<volatile uint32_t*>(&us.thr_key);
+        const int n = warp_compact_ge(wk, wi, wcnt, T);
+        uint32_t base = 0;
+        if (lane == 0 && n) base = atomicAdd(&p.row_cnt[row], (uint32_t)n);
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (base + (uint32_t)n > (uint32_t)p.row_cap) {
+            fl |= FLAG_OVERFLOW;
+        } else {
+            uint64_t* dst = p.row_cand + row * (int64_t)p.row_cap + base;
+            for (int i = lane; i < n; i += 32) dst[i] = ((uint64_t)wk[i] << 32) | (uint32_t)wi[i];
+        }
+        if (__any_sync(0xffffffffu, nan)) fl |= FLAG_NAN;
+        if (lane == 0 && fl) atomicOr(&p.row_flag[row], fl);
+        // The last warp out recycles the slot for unit j + SLOTS (no warp can be
+        // that far ahead: the ring keeps them within STAGES tiles of each other).
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            if (atomicAdd(&us.done, 1u) == NWARPS - 1) {
+                us.thr_key = 0u;
+                for (int w = 0; w < NWARPS; ++w) us.pub[w] = 0u;
+                __threadfence_block();
+                us.done = 0u;
+            }
+        }
+        __syncwarp();
+    }
+}
+
+// One warp per row: select, register sort, tie check, draw; rows that need the
+// exact replay go to the exact kernel's list.
+constexpr int F_WARPS = 8;
+struct FinishWarpSmem {
+    uint32_t keys[FCAP];
+    int32_t idx[FCAP];
+    uint32_t hist[256];
+    double pbuf[KSPLIT_K];
+    Ent e[KSPLIT_K];
+};
+
+__device__ void warp_draw(const Params& p, int64_t row, const Ent* e, int k, double* pbuf) {
+    const int lane = threadIdx.x & 31;
+    if (p.topk_idx)
+        for (int i = lane; i < k; i += 32) p.topk_idx[row * k + i] = e[i].i;
+    const double T = p.temperature;
+    bool greedy = (T <= 0.0);
+    double sum = 0.0;
+    if (!greedy) {
+        const double maxs = (double)e[0].v;
+        for (int i = lane; i < k; i += 32) pbuf[i] = exp(((double)e[i].v - maxs) / T);
+        __syncwarp();
+        if (lane == 0) sum = seq_sum(pbuf, k);
+        sum = __shfl_sync(0xffffffffu, sum, 0);
+        greedy = (sum <= 0.0);
+    }
+    if (greedy) {
+        if (p.topk_prob)
+            for (int i = lane; i < k; i += 32) p.topk_prob[row * k + i] = (i == 0) ? 1.0 : 0.0;
+        if (lane == 0) p.next[row] = e[0].i;
+        return;
+    }
+    for (int i = lane; i < k; i += 32) {
+        const double q = pbuf[i] / sum;
+        pbuf[i] = q;
+        if (p.topk_prob) p.topk_prob[row * k + i] = q;
+    }
+    __syncwarp();
+    int n = 0;
+    double s2 = 0.0;
+    if (lane == 0) {
+        n = truncate_p(pbuf, k, p.top_p, p.min_p);
+        s2 = (n >= 2) ? seq_sum(pbuf, n) : 0.0;
+    }
+    n = __shfl_sync(0xffffffffu, n, 0);
+    s2 = __shfl_sync(0xffffffffu, s2, 0);
+    __syncwarp();
+    if (n < 2) {  // discrete_distribution with fewer than two weights returns 0
+        if (lane == 0) p.next[row] = e[0].i;
+        return;
+    }
+    for (int i = lane; i < n; i += 32) pbuf[i] = pbuf[i] / s2;
+    __syncwarp();
+    if (lane == 0) p.next[row] = e[cdf_pick(pbuf, n, p.u[row])].i;
+}
+
+__global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
+    extern __shared__ __align__(16) unsigned char fsmem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    FinishWarpSmem& w = reinterpret_cast<FinishWarpSmem*>(fsmem)[warp];
+    const int64_t row = (int64_t)blockIdx.x * F_WARPS + warp;
+    if (row >= p.rows) return;
+    const int k = p.k_use;
+    uint32_t flags = p.row_flag[row];
+    const uint32_t cnt_all = p.row_cnt[row];
+    bool exact = (flags & (FLAG_NAN | FLAG_OVERFLOW)) != 0 || cnt_all > (uint32_t)FCAP ||
+                 cnt_all > (uint32_t)p.row_cap || cnt_all < (uint32_t)k;
+    if (!(flags & FLAG_TIMEOUT) && !exact) {
+        int cnt = (int)cnt_all;
+        const uint64_t* src = p.row_cand + row * (int64_t)p.row_cap;
+        for (int i = lane; i < cnt; i += 32) {
+            const uint64_t v = src[i];
+            w.keys[i] = (uint32_t)(v >> 32);
+            w.idx[i] = (int32_t)(uint32_t)v;
+        }
+        __syncwarp();
+        if (cnt > k) {
+            const uint32_t kth = warp_select_kth(w.keys, cnt, k, w.hist);
+            cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
+            exact = (cnt != k);  // a tie straddles the cut
+        }
+        if (!exact) {
+            uint64_t b0 = lane < k ? ((uint64_t)w.keys[lane] << 32) | (uint32_t)w.idx[lane] : 0ull;
+            uint64_t b1 = lane + 32 < k ? ((uint64_t)w.keys[lane + 32] << 32) | (uint32_t)w.idx[lane + 32] : 0ull;
+            warp_sort64_desc(b0, b1);
+            const uint64_t first1 = __shfl_sync(0xffffffffu, b1, 0);
+            const uint64_t dn0 = __shfl_down_sync(0xffffffffu, b0, 1);
+            const uint64_t n1 = __shfl_down_sync(0xffffffffu, b1, 1);
+            const uint64_t n0 = (lane == 31) ? first1 : dn0;
+            const bool tie = (lane < k - 1 && (b0 >> 32) == (n0 >> 32)) ||
+                             (lane + 32 < k - 1 && (b1 >> 32) == (n1 >> 32));
+            exact = __any_sync(0xffffffffu, tie);
+            if (!exact) {
+                if (lane < k) w.e[lane] = Ent{fkey_inv((uint32_t)(b0 >> 32)), (int32_t)(uint32_t)b0};
+                if (lane + 32 < k) w.e[lane + 32] = Ent{fkey_inv((uint32_t)(b1 >> 32)), (int32_t)(uint32_t)b1};
+                __syncwarp();
+                warp_draw(p, row, w.e, k, w.pbuf);
+            }
+        }
+    }
+    if (lane == 0) {
+        if (flags & FLAG_TIMEOUT) {
+            p.next[row] = -1;
+            atomicOr(p.status, flags);
+        } else if (exact) {
+            p.xrows[atomicAdd(p.xcount, 1u)] = (int32_t)row;
+        }
+        if (p.row_flags) p.row_flags[row] = flags | ((exact && !(flags & FLAG_TIMEOUT)) ? FLAG_EXACT : 0u);
+    }
+}
+
+// One CTA per handed-over row (grid-stride over the list).
+__global__ void __launch_bounds__(NT) exact_rows_kernel(Params p) {
+    extern __shared__ __align__(128) unsigned char esmem[];
+    Misc& sm = *reinterpret_cast<Misc*>(esmem + REGION_BYTES);
+    const uint32_t n = *reinterpret_cast<volatile uint32_t*>(p.xcount);
+    for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
+        const int64_t row = p.xrows[i];
+        const uint32_t f = p.row_flag[row];
+        exact_row(p, row, (f & FLAG_NAN) ? 1 : 0, esmem, sm);
+    }
+}
+
+size_t stream_smem_bytes() { return S_SMEM; }
+
+cudaError_t stream_path_configure(int* blocks_per_sm) {
+    cudaError_t e = cudaFuncSetAttribute(stream_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(finish_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(FinishWarpSmem) * F_WARPS));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(exact_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(REGION_BYTES + sizeof(Misc)));
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, stream_select_kernel, NT_WS, S_SMEM);
+}
+
+cudaError_t stream_path_launch(const Params& p, int grid, int exact_grid, cudaStream_t stream) {
+    stream_select_kernel<<<grid, NT_WS, S_SMEM, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    finish_rows_kernel<<<(unsigned)((p.rows + F_WARPS - 1) / F_WARPS), F_WARPS * 32, sizeof(FinishWarpSmem) * F_WARPS,
+                         stream>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    exact_rows_kernel<<<exact_grid, NT, REGION_BYTES + sizeof(Misc), stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace mxs

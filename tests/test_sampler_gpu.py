@@ -15,13 +15,18 @@ from test_oracle import GOLDEN_CASES, check_against_golden, golden_logits
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["warp_specialised", "block_sync"], autouse=True)
+@pytest.fixture(params=["split", "fused_ws", "block_sync"], autouse=True)
 def kernel_variant(request, monkeypatch):
-    """Run every parity case on both streaming kernels."""
-    if request.param == "block_sync":
-        monkeypatch.setenv("MXS_SAMPLER_BLOCK_PATH", "1")
+    """Run every parity case on each kernel path: the three-kernel path
+    (stream -> finish -> exact, default for k <= 64), the one-launch
+    warp-specialised kernel, and the CTA-synchronous kernel."""
+    monkeypatch.delenv("MXS_SAMPLER_BLOCK_PATH", raising=False)
+    if request.param == "fused_ws":
+        monkeypatch.setenv("MXS_SAMPLER_PATH", "fused")
+    elif request.param == "block_sync":
+        monkeypatch.setenv("MXS_SAMPLER_PATH", "block")
     else:
-        monkeypatch.delenv("MXS_SAMPLER_BLOCK_PATH", raising=False)
+        monkeypatch.delenv("MXS_SAMPLER_PATH", raising=False)
     return request.param
 
 
