@@ -72,6 +72,10 @@ __device__ __forceinline__ void stream_shrink(uint32_t* wk, int32_t* wi, int& wc
     wcnt = warp_compact_ge(wk, wi, wcnt, *reinterpret_cast<volatile uint32_t*>(&us.thr_key));
 }
 
+// The bound a key word stands for: 0 means "no bound yet" (-inf), not the
+// NaN that key 0 would decode to.
+__device__ __forceinline__ float bound_of(uint32_t key) { return key ? fkey_inv(key) : -INFINITY; }
+
 // Warp-wide bitonic sort of one key per lane, descending.
 __device__ __forceinline__ uint32_t warp_sort32_desc(uint32_t v) {
     const int lane = threadIdx.x & 31;
@@ -168,6 +172,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
         int wcnt = 0, nan = 0, ntrig = wtrig;
         uint32_t fl = dead ? FLAG_TIMEOUT : 0u;
         bool stopped = false;
+        float wseed = -INFINITY;  // this warp's own bound from its first tile
         for (int t = 0; t < nt; ++t, ++cseq) {
             const int64_t a = ((int64_t)c * TPC + t) * TILE;
             const int len = (int)(min(a + TILE, V) - a);
@@ -206,22 +211,41 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             const float mxn = fmax_nan(fmax_nan(mx8[0], mx8[1]), fmax_nan(mx8[2], mx8[3]));
             nan |= (mxn != mxn);
             if (t == 0) {
-                // Seed: this warp's m-th largest lane maximum (m distinct logits
-                // of the slice are >= it); lanes without logits offer nothing.
-                float mx = -INFINITY;
+                // Seeds from the unit's first tile. Per lane: the largest and
+                // second largest logit (64 distinct logits per warp).
+                //  - own bound: the k-th largest of those 64 (k <= 64 logits are >= it);
+                //  - published: the m-th largest lane maximum, m = ceil(k / NWARPS);
+                //    the smallest over all warps bounds the unit (see stream_shrink).
+                float m1 = -INFINITY, m2 = -INFINITY;
 #pragma unroll
-                for (int b = 0; b < 16; ++b) mx = vv[b] > mx ? vv[b] : mx;
-                const uint32_t key = valid ? fkey(mx) : 0u;
-                const uint32_t sorted = warp_sort32_desc(key);
-                const uint32_t km = __shfl_sync(0xffffffffu, sorted, m - 1);
-                if (lane == 0 && km) atomicMax(&us.pub[warp], km);
+                for (int b = 0; b < 16; ++b) {
+                    if ((valid >> b) & 1u) {
+                        const float x = vv[b];
+                        if (x > m1) {
+                            m2 = m1;
+                            m1 = x;
+                        } else if (x > m2) {
+                            m2 = x;
+                        }
+                    }
+                }
+                const int nv = __popc(valid);
+                uint64_t s0 = (nv >= 1) ? (uint64_t)fkey(m1) << 32 : 0ull;
+                uint64_t s1 = (nv >= 2) ? (uint64_t)fkey(m2) << 32 : 0ull;
+                warp_sort64_desc(s0, s1);
+                const uint64_t kth = (k <= 32) ? __shfl_sync(0xffffffffu, s0, k - 1) : __shfl_sync(0xffffffffu, s1, k - 33);
+                wseed = bound_of((uint32_t)(kth >> 32));
+                const uint32_t km = warp_sort32_desc((nv >= 1) ? fkey(m1) : 0u);
+                const uint32_t pm = __shfl_sync(0xffffffffu, km, m - 1);
+                if (lane == 0 && pm) atomicMax(&us.pub[warp], pm);
                 __syncwarp();
                 uint32_t mn = (lane < NWARPS) ? *reinterpret_cast<volatile uint32_t*>(&us.pub[lane]) : 0xFFFFFFFFu;
 #pragma unroll
                 for (int d = 16; d > 0; d >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, d));
                 if (lane == 0 && mn) atomicMax(&us.thr_key, mn);
             }
-            const float thr = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
+            float thr = bound_of(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
+            thr = thr > wseed ? thr : wseed;
             if (!stopped && __any_sync(0xffffffffu, mxn >= thr)) {
                 auto pass_bits = [&](float th) -> uint32_t {
                     uint32_t mm = 0;
@@ -238,7 +262,8 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 int tot = __shfl_sync(0xffffffffu, incl, 31);
                 if (wcnt + tot > SW_CAP) {
                     stream_shrink(wk, wi, wcnt, k, whist, us);
-                    mm = pass_bits(fkey_inv(*reinterpret_cast<volatile uint32_t*>(&us.thr_key)));
+                    float thr2 = bound_of(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
+                    mm = pass_bits(thr2 > wseed ? thr2 : wseed);
                     cc = __popc(mm);
                     incl = warp_incl_scan(cc);
                     tot = __shfl_sync(0xffffffffu, incl, 31);
