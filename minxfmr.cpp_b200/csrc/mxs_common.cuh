@@ -21,7 +21,7 @@ constexpr int CAP = 4096;               // candidate buffer entries
 constexpr int KFAST = 2048;             // largest k the streaming path selects
 constexpr int SORTMAX = 2048;           // largest candidate set the final sort takes
 constexpr int HEAP_SMEM_MAX = 2048;     // exact path keeps its heap in shared memory up to here
-constexpr int XTILE = 2048;             // exact path: elements filtered per replay step
+constexpr int XTILE = 2048;             // exact path: largest replay step (logits)
 
 // Row flag bits (optional per-row output).
 constexpr uint32_t FLAG_EXACT = 1u;     // row resolved by the exact heap replay
@@ -73,8 +73,8 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 // Bulk copy of `bytes` (multiple of 16) from 16-byte aligned global memory into
-// 16-byte aligned shared memory; the read is hinted evict-first in L2 because
-// every logit is read exactly once.
+// 16-byte aligned shared memory, with an L2 cache policy. (An evict-first hint
+// measured ~5% slower than evict-normal for this streaming read on B200.)
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                          uint64_t policy) {
     asm volatile(
@@ -83,9 +83,9 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
-__device__ __forceinline__ uint64_t policy_evict_first() {
+__device__ __forceinline__ uint64_t policy_evict_normal() {
     uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {

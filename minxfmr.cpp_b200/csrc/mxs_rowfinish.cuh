@@ -182,29 +182,44 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
         } else {
             // Steps grow from NT to XTILE logits: the root starts as the
             // smallest of the first k logits and rises fast, so short early
-            // steps keep the serial offers near k * (1 + ln(V / k)).
+            // steps keep the serial offers near k * (1 + ln(V / k)). The next
+            // step's logits are loaded while thread 0 makes the offers.
             constexpr int PER = XTILE / NT;
             int per = 1;
-            for (int64_t base = k; base < V; base += (int64_t)per * NT, per = per < PER ? 2 * per : PER) {
+            int64_t base = k;
+            float cur[PER], nxt[PER];
+#pragma unroll
+            for (int q = 0; q < PER; ++q) {
+                const int64_t jj = base + (int64_t)tid * per + q;
+                cur[q] = (q < per && jj < V) ? x[jj] : -INFINITY;
+            }
+            while (base < V) {
                 const float r0 = h[0].v;
-                float xv[PER];
                 int c = 0;
 #pragma unroll
-                for (int q = 0; q < PER; ++q) {
-                    const int64_t j = base + (int64_t)tid * per + q;
-                    xv[q] = (q < per && j < V) ? x[j] : r0;
-                    c += (xv[q] > r0) ? 1 : 0;
-                }
+                for (int q = 0; q < PER; ++q) c += (q < per && base + (int64_t)tid * per + q < V && cur[q] > r0) ? 1 : 0;
                 int total;
                 int pos = block_excl_scan(c, sm, &total);
 #pragma unroll
                 for (int q = 0; q < PER; ++q) {
-                    if (xv[q] > r0) xl[pos++] = Ent{xv[q], (int32_t)(base + (int64_t)tid * per + q)};
+                    const int64_t jj = base + (int64_t)tid * per + q;
+                    if (q < per && jj < V && cur[q] > r0) xl[pos++] = Ent{cur[q], (int32_t)jj};
+                }
+                const int64_t nbase = base + (int64_t)per * NT;
+                const int nper = per < PER ? 2 * per : PER;
+#pragma unroll
+                for (int q = 0; q < PER; ++q) {
+                    const int64_t jj = nbase + (int64_t)tid * nper + q;
+                    nxt[q] = (q < nper && jj < V) ? x[jj] : -INFINITY;
                 }
                 csync();
                 if (tid == 0)
                     for (int i = 0; i < total; ++i) heap_offer(h, k, xl[i]);
                 csync();
+#pragma unroll
+                for (int q = 0; q < PER; ++q) cur[q] = nxt[q];
+                base = nbase;
+                per = nper;
             }
         }
     }

@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
     if (TMA && tid == 0) {
         for (int s = 0; s < STAGES; ++s) mbar_init(&sm.bar[s], 1);
         fence_mbar_init();
-        pol = policy_evict_first();
+        pol = policy_evict_normal();
     }
     csync();
     auto unit_tiles = [&](int64_t u) -> int {
@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
     if (warp == NWARPS) {
         // Producer warp: lane 0 streams every tile of every unit of this CTA.
         if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
+            const uint64_t pol = policy_evict_normal();
             uint32_t seq = 0;
             bool ok = true;
             for (int64_t j = 0; j < nj && ok; ++j) {

@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
 
     if (warp == NWARPS) {  // producer
         if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
+            const uint64_t pol = policy_evict_normal();
             uint32_t seq = 0;
             for (int64_t j = 0; j < nj; ++j) {
                 const int64_t u = blockIdx.x + j * G;
@@ -261,28 +261,37 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 int incl = warp_incl_scan(cc);
                 int tot = __shfl_sync(0xffffffffu, incl, 31);
                 if (wcnt + tot > SW_CAP) {
-                    stream_shrink(wk, wi, wcnt, k, whist, us);
-                    float thr2 = bound_of(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
-                    mm = pass_bits(thr2 > wseed ? thr2 : wseed);
-                    cc = __popc(mm);
-                    incl = warp_incl_scan(cc);
-                    tot = __shfl_sync(0xffffffffu, incl, 31);
-                    if (wcnt + tot > SW_CAP) {  // massive ties: the exact replay takes the row
-                        stopped = true;
-                        fl |= FLAG_OVERFLOW;
-                        mm = 0;
-                        tot = 0;
+                    // Does not fit (no bound yet, or a loose one): take the
+                    // four float4 groups one at a time, shrinking in between.
+                    for (int q = 0; q < 4 && !stopped; ++q) {
+                        stream_shrink(wk, wi, wcnt, k, whist, us);
+                        float th = bound_of(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
+                        th = th > wseed ? th : wseed;
+                        uint32_t mq = (pass_bits(th) >> (4 * q)) & 0xFu;
+                        const int cq = __popc(mq);
+                        const int iq = warp_incl_scan(cq);
+                        const int tq = __shfl_sync(0xffffffffu, iq, 31);
+                        if (wcnt + tq > SW_CAP) {  // massive ties: the exact replay takes the row
+                            stopped = true;
+                            fl |= FLAG_OVERFLOW;
+                            break;
+                        }
+                        int pq = wcnt + iq - cq;
+                        while (mq) {
+                            const int b = 4 * q + __ffs(mq) - 1;
+                            mq &= mq - 1;
+                            const int e = 4 * (warp * 128 + lane + 32 * q) + (b & 3);
+                            const float v = (e < bulk_n) ? st[e] : xr[a + e];
+                            wk[pq] = fkey(v);
+                            wi[pq] = (int32_t)(a + e);
+                            ++pq;
+                        }
+                        wcnt += tq;
                     }
-                }
-                int pos = wcnt + incl - cc;
-                while (mm) {
-                    const int b = __ffs(mm) - 1;
-                    mm &= mm - 1;
-                    const int e = 4 * (warp * 128 + lane + 32 * (b >> 2)) + (b & 3);
-                    const float v = (e < bulk_n) ? st[e] : xr[a + e];
-                    wk[pos] = fkey(v);
-                    wi[pos] = (int32_t)(a + e);
-                    ++pos;
+                    mm = 0;
+                    cc = 0;
+                    incl = 0;
+                    tot = 0;
                 }
                 wcnt += tot;
                 if (wcnt > ntrig) {
