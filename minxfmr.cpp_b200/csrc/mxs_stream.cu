@@ -293,6 +293,16 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     incl = 0;
                     tot = 0;
                 }
+                int pos = wcnt + incl - cc;
+                while (mm) {
+                    const int b = __ffs(mm) - 1;
+                    mm &= mm - 1;
+                    const int e = 4 * (warp * 128 + lane + 32 * (b >> 2)) + (b & 3);
+                    const float v = (e < bulk_n) ? st[e] : xr[a + e];
+                    wk[pos] = fkey(v);
+                    wi[pos] = (int32_t)(a + e);
+                    ++pos;
+                }
                 wcnt += tot;
                 if (wcnt > ntrig) {
                     stream_shrink(wk, wi, wcnt, k, whist, us);
