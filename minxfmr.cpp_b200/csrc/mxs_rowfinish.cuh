@@ -180,46 +180,39 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
                 for (int64_t j = k; j < V; ++j) heap_offer(h, k, Ent{x[j], (int32_t)j});
             csync();
         } else {
-            // Steps grow from NT to XTILE logits: the root starts as the
-            // smallest of the first k logits and rises fast, so short early
-            // steps keep the serial offers near k * (1 + ln(V / k)). The next
-            // step's logits are loaded while thread 0 makes the offers.
-            constexpr int PER = XTILE / NT;
-            int per = 1;
+            // Geometric steps: step s covers as many logits as came before it
+            // (256, 512, ..., at most 65,536). Only logits above the root at
+            // the step's start can enter, so a step yields about k offers
+            // whatever its size, and the whole row takes ~10 steps. Each
+            // thread filters a contiguous range, so the order of the offers
+            // is the logits' order. A step that yields more than XTILE
+            // candidates is taken again at a quarter of the size.
             int64_t base = k;
-            float cur[PER], nxt[PER];
-#pragma unroll
-            for (int q = 0; q < PER; ++q) {
-                const int64_t jj = base + (int64_t)tid * per + q;
-                cur[q] = (q < per && jj < V) ? x[jj] : -INFINITY;
-            }
+            int64_t size = NT;
             while (base < V) {
+                const int64_t len = min(size, V - base);
+                const int64_t per = (len + NT - 1) / NT;
+                const int64_t lo = base + min((int64_t)tid * per, len);
+                const int64_t hi = base + min((int64_t)(tid + 1) * per, len);
                 const float r0 = h[0].v;
                 int c = 0;
-#pragma unroll
-                for (int q = 0; q < PER; ++q) c += (q < per && base + (int64_t)tid * per + q < V && cur[q] > r0) ? 1 : 0;
+                for (int64_t jj = lo; jj < hi; ++jj) c += (x[jj] > r0) ? 1 : 0;
                 int total;
                 int pos = block_excl_scan(c, sm, &total);
-#pragma unroll
-                for (int q = 0; q < PER; ++q) {
-                    const int64_t jj = base + (int64_t)tid * per + q;
-                    if (q < per && jj < V && cur[q] > r0) xl[pos++] = Ent{cur[q], (int32_t)jj};
+                if (total > XTILE) {  // too many at once: retry smaller (256 always fits)
+                    size = max((int64_t)NT, len / 4);
+                    continue;
                 }
-                const int64_t nbase = base + (int64_t)per * NT;
-                const int nper = per < PER ? 2 * per : PER;
-#pragma unroll
-                for (int q = 0; q < PER; ++q) {
-                    const int64_t jj = nbase + (int64_t)tid * nper + q;
-                    nxt[q] = (q < nper && jj < V) ? x[jj] : -INFINITY;
+                for (int64_t jj = lo; jj < hi; ++jj) {
+                    const float xv = x[jj];
+                    if (xv > r0) xl[pos++] = Ent{xv, (int32_t)jj};
                 }
                 csync();
                 if (tid == 0)
                     for (int i = 0; i < total; ++i) heap_offer(h, k, xl[i]);
                 csync();
-#pragma unroll
-                for (int q = 0; q < PER; ++q) cur[q] = nxt[q];
-                base = nbase;
-                per = nper;
+                base += len;
+                size = min(2 * size, (int64_t)65536);
             }
         }
     }
