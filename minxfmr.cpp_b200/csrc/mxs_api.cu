@@ -95,6 +95,10 @@ int path_override() {
     return 0;
 }
 
+// Candidate list entries per row: a row split over S chunks gets up to 256 per
+// chunk (each chunk keeps at least k of its own logits).
+int split_row_cap(int S) { return std::max(mxs::SPLIT_ROW_CAP, 256 * S); }
+
 bool use_split(int64_t vocab, int64_t ld, const float* logits, int k_use) {
     const bool tma = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && (ld % 4 == 0);
     (void)vocab;
@@ -144,7 +148,7 @@ Plan make_plan(const Device& d, int64_t rows, int64_t vocab, int k_use, bool mer
         pl.off_xrows = o;
         o = align_up(o + sizeof(int32_t) * (size_t)rows, 256);
         pl.off_rcand = o;
-        o = align_up(o + sizeof(uint64_t) * (size_t)rows * mxs::SPLIT_ROW_CAP, 256);
+        o = align_up(o + sizeof(uint64_t) * (size_t)rows * split_row_cap(pl.S), 256);
     } else if (pl.S > 1) {
         o = align_up(o + sizeof(uint32_t) * (size_t)rows * pl.S, 256);
         pl.off_cand = o;
@@ -189,7 +193,7 @@ void fill_workspace(Params& p, const Plan& pl, void* ws) {
         p.row_cand = reinterpret_cast<uint64_t*>(b + pl.off_rcand);
         p.row_cnt = reinterpret_cast<uint32_t*>(b + pl.off_rcnt);
         p.row_flag = reinterpret_cast<uint32_t*>(b + pl.off_rflag);
-        p.row_cap = mxs::SPLIT_ROW_CAP;
+        p.row_cap = split_row_cap(pl.S);
         p.xcount = reinterpret_cast<uint32_t*>(b + pl.off_xcount);
         p.xrows = reinterpret_cast<int32_t*>(b + pl.off_xrows);
     }

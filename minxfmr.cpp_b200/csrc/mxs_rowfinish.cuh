@@ -183,29 +183,61 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
             // Geometric steps: step s covers as many logits as came before it
             // (256, 512, ..., at most 65,536). Only logits above the root at
             // the step's start can enter, so a step yields about k offers
-            // whatever its size, and the whole row takes ~10 steps. Each
-            // thread filters a contiguous range, so the order of the offers
-            // is the logits' order. A step that yields more than XTILE
-            // candidates is taken again at a quarter of the size.
+            // whatever its size, and the whole row takes ~10 steps. Each warp
+            // filters a contiguous segment of the step, 32 consecutive logits
+            // per load, and ballots keep the offers in the logits' order. A
+            // step that yields more than XTILE candidates is taken again at a
+            // quarter of the size.
+            const int lane = tid & 31, w = tid >> 5;
             int64_t base = k;
             int64_t size = NT;
             while (base < V) {
                 const int64_t len = min(size, V - base);
-                const int64_t per = (len + NT - 1) / NT;
-                const int64_t lo = base + min((int64_t)tid * per, len);
-                const int64_t hi = base + min((int64_t)(tid + 1) * per, len);
+                const int64_t seg = (len + NWARPS - 1) / NWARPS;
+                const int64_t lo = base + min((int64_t)w * seg, len);
+                const int64_t hi = base + min((int64_t)(w + 1) * seg, len);
                 const float r0 = h[0].v;
                 int c = 0;
-                for (int64_t jj = lo; jj < hi; ++jj) c += (x[jj] > r0) ? 1 : 0;
-                int total;
-                int pos = block_excl_scan(c, sm, &total);
+                for (int64_t g = lo; g < hi; g += 128) {
+                    float xv[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int64_t jj = g + 32 * q + lane;
+                        xv[q] = (jj < hi) ? x[jj] : r0;
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) c += __popc(__ballot_sync(0xffffffffu, xv[q] > r0));
+                }
+                // c is the warp's count (same in every lane); scan over warps
+                if (lane == 0) sm.warp_tot[w] = c;
+                csync();
+                int off = 0, total = 0;
+#pragma unroll
+                for (int i2 = 0; i2 < NWARPS; ++i2) {
+                    const int t2 = sm.warp_tot[i2];
+                    off += (i2 < w) ? t2 : 0;
+                    total += t2;
+                }
+                csync();
                 if (total > XTILE) {  // too many at once: retry smaller (256 always fits)
                     size = max((int64_t)NT, len / 4);
                     continue;
                 }
-                for (int64_t jj = lo; jj < hi; ++jj) {
-                    const float xv = x[jj];
-                    if (xv > r0) xl[pos++] = Ent{xv, (int32_t)jj};
+                const uint32_t lt = (1u << lane) - 1u;
+                for (int64_t g = lo; g < hi; g += 128) {
+                    float xv[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int64_t jj = g + 32 * q + lane;
+                        xv[q] = (jj < hi) ? x[jj] : r0;
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const bool pass = xv[q] > r0;
+                        const uint32_t bal = __ballot_sync(0xffffffffu, pass);
+                        if (pass) xl[off + __popc(bal & lt)] = Ent{xv[q], (int32_t)(g + 32 * q + lane)};
+                        off += __popc(bal);
+                    }
                 }
                 csync();
                 if (tid == 0)

@@ -25,7 +25,7 @@ constexpr int SW_CAP = 256;         // candidates per consumer warp
 constexpr int SLOTS = 8;            // per-unit state ring (> the STAGES a warp can run ahead)
 constexpr int FCAP = 1024;          // candidates per row the finish warp takes
 static_assert(KSPLIT_K == KSPLIT, "KSPLIT must match the register sort");
-static_assert(FCAP == SPLIT_ROW_CAP, "a finish warp takes a whole row list");
+
 
 struct UnitState {
     uint32_t thr_key;        // shared bound (order-preserving key), only grows
@@ -407,21 +407,47 @@ __global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
     const int k = p.k_use;
     uint32_t flags = p.row_flag[row];
     const uint32_t cnt_all = p.row_cnt[row];
-    bool exact = (flags & (FLAG_NAN | FLAG_OVERFLOW)) != 0 || cnt_all > (uint32_t)FCAP ||
-                 cnt_all > (uint32_t)p.row_cap || cnt_all < (uint32_t)k;
+    bool exact = (flags & (FLAG_NAN | FLAG_OVERFLOW)) != 0 || cnt_all > (uint32_t)p.row_cap ||
+                 cnt_all < (uint32_t)k;
     if (!(flags & FLAG_TIMEOUT) && !exact) {
-        int cnt = (int)cnt_all;
+        // Take the list in batches of 32 against a running bound (the k-th
+        // largest key held once the buffer has filled), so lists longer than
+        // the buffer (a row split over many chunks) still fit.
         const uint64_t* src = p.row_cand + row * (int64_t)p.row_cap;
-        for (int i = lane; i < cnt; i += 32) {
-            const uint64_t v = src[i];
-            w.keys[i] = (uint32_t)(v >> 32);
-            w.idx[i] = (int32_t)(uint32_t)v;
+        const uint32_t lt = (1u << lane) - 1u;
+        int cnt = 0;
+        uint32_t bound = 0u;
+        for (int i0 = 0; i0 < (int)cnt_all; i0 += 32) {
+            const int i = i0 + lane;
+            uint64_t v = 0;
+            bool take = false;
+            if (i < (int)cnt_all) {
+                v = src[i];
+                take = (uint32_t)(v >> 32) >= bound;
+            }
+            const uint32_t bal = __ballot_sync(0xffffffffu, take);
+            if (take) {
+                const int pos = cnt + __popc(bal & lt);
+                w.keys[pos] = (uint32_t)(v >> 32);
+                w.idx[pos] = (int32_t)(uint32_t)v;
+            }
+            cnt += __popc(bal);
+            __syncwarp();
+            if (cnt > FCAP - 32) {
+                bound = warp_select_kth(w.keys, cnt, k, w.hist);
+                cnt = warp_compact_ge(w.keys, w.idx, cnt, bound);
+                if (cnt > FCAP - 32) {  // massive ties
+                    exact = true;
+                    break;
+                }
+            }
         }
-        __syncwarp();
-        if (cnt > k) {
+        if (!exact && cnt > k) {
             const uint32_t kth = warp_select_kth(w.keys, cnt, k, w.hist);
             cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
             exact = (cnt != k);  // a tie straddles the cut
+        } else if (cnt < k) {
+            exact = true;
         }
         if (!exact) {
             uint64_t b0 = lane < k ? ((uint64_t)w.keys[lane] << 32) | (uint32_t)w.idx[lane] : 0ull;
