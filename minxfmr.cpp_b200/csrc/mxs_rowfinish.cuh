@@ -184,11 +184,14 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
             // (256, 512, ..., at most 65,536). Only logits above the root at
             // the step's start can enter, so a step yields about k offers
             // whatever its size, and the whole row takes ~10 steps. Each warp
-            // filters a contiguous segment of the step, 32 consecutive logits
-            // per load, and ballots keep the offers in the logits' order. A
-            // step that yields more than XTILE candidates is taken again at a
-            // quarter of the size.
+            // filters a contiguous segment of the step in one pass (8 loads of
+            // 32 consecutive logits in flight) into its own slot of the replay
+            // list; thread 0 then offers slot 0, slot 1, ... in the logits'
+            // order. A slot that overflows retakes the step at a quarter size.
+            constexpr int SLOT = XTILE / NWARPS;
             const int lane = tid & 31, w = tid >> 5;
+            const uint32_t lt = (1u << lane) - 1u;
+            Ent* slot = xl + w * SLOT;
             int64_t base = k;
             int64_t size = NT;
             while (base < V) {
@@ -198,50 +201,35 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
                 const int64_t hi = base + min((int64_t)(w + 1) * seg, len);
                 const float r0 = h[0].v;
                 int c = 0;
-                for (int64_t g = lo; g < hi; g += 128) {
-                    float xv[4];
+                for (int64_t g = lo; g < hi; g += 256) {
+                    float xv[8];
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
+                    for (int q = 0; q < 8; ++q) {
                         const int64_t jj = g + 32 * q + lane;
                         xv[q] = (jj < hi) ? x[jj] : r0;
                     }
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) c += __popc(__ballot_sync(0xffffffffu, xv[q] > r0));
+                    for (int q = 0; q < 8; ++q) {
+                        const bool pass = xv[q] > r0;
+                        const uint32_t bal = __ballot_sync(0xffffffffu, pass);
+                        const int at = c + __popc(bal & lt);
+                        if (pass && at < SLOT) slot[at] = Ent{xv[q], (int32_t)(g + 32 * q + lane)};
+                        c += __popc(bal);
+                    }
                 }
-                // c is the warp's count (same in every lane); scan over warps
                 if (lane == 0) sm.warp_tot[w] = c;
-                csync();
-                int off = 0, total = 0;
-#pragma unroll
-                for (int i2 = 0; i2 < NWARPS; ++i2) {
-                    const int t2 = sm.warp_tot[i2];
-                    off += (i2 < w) ? t2 : 0;
-                    total += t2;
-                }
-                csync();
-                if (total > XTILE) {  // too many at once: retry smaller (256 always fits)
+                const int over = csync_or(c > SLOT);
+                if (over) {  // retry smaller (NT logits always fit: 32 per warp)
                     size = max((int64_t)NT, len / 4);
                     continue;
                 }
-                const uint32_t lt = (1u << lane) - 1u;
-                for (int64_t g = lo; g < hi; g += 128) {
-                    float xv[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int64_t jj = g + 32 * q + lane;
-                        xv[q] = (jj < hi) ? x[jj] : r0;
-                    }
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const bool pass = xv[q] > r0;
-                        const uint32_t bal = __ballot_sync(0xffffffffu, pass);
-                        if (pass) xl[off + __popc(bal & lt)] = Ent{xv[q], (int32_t)(g + 32 * q + lane)};
-                        off += __popc(bal);
+                if (tid == 0) {
+                    for (int w2 = 0; w2 < NWARPS; ++w2) {
+                        const Ent* sl = xl + w2 * SLOT;
+                        const int n2 = sm.warp_tot[w2];
+                        for (int i = 0; i < n2; ++i) heap_offer(h, k, sl[i]);
                     }
                 }
-                csync();
-                if (tid == 0)
-                    for (int i = 0; i < total; ++i) heap_offer(h, k, xl[i]);
                 csync();
                 base += len;
                 size = min(2 * size, (int64_t)65536);
