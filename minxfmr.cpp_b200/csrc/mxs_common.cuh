@@ -128,7 +128,12 @@ __shared__ unsigned long long s_mxs_prof[PROF_PHASES];  // per CTA, flushed once
             for (int i_ = 0; i_ < mxs::PROF_PHASES; ++i_)                            \
                 mxs::g_mxs_prof[blockIdx.x][i_] += mxs::s_mxs_prof[i_];              \
     } while (0)
+#define MXS_PROF_COUNT(ph, n)                                                        \
+    do {                                                                             \
+        if (threadIdx.x == 0) mxs::s_mxs_prof[ph] += (unsigned long long)(n);        \
+    } while (0)
 #else
+#define MXS_PROF_COUNT(ph, n) (void)0
 #define MXS_PROF_T0(v) (void)0
 #define MXS_PROF_ADD(ph, v) (void)0
 #define MXS_PROF_BEGIN() (void)0

@@ -170,10 +170,12 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
         for (int64_t j = tid; j < V; j += NT) has |= (x[j] != x[j]);
         nan_state = csync_or(has) ? 1 : 0;
     }
+    MXS_PROF_T0(tb);
     for (int i = tid; i < k; i += NT) h[i] = Ent{x[i], i};
     csync();
     if (tid == 0) heap_build(h, k);
     csync();
+    MXS_PROF_ADD(3, tb);
     if (k < V) {
         if (nan_state) {
             if (tid == 0)
@@ -200,6 +202,7 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
                 const int64_t lo = base + min((int64_t)w * seg, len);
                 const int64_t hi = base + min((int64_t)(w + 1) * seg, len);
                 const float r0 = h[0].v;
+                MXS_PROF_T0(tfl);
                 int c = 0;
                 for (int64_t g = lo; g < hi; g += 256) {
                     float xv[8];
@@ -223,6 +226,8 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
                     size = max((int64_t)NT, len / 4);
                     continue;
                 }
+                MXS_PROF_ADD(0, tfl);
+                MXS_PROF_T0(tof);
                 if (tid == 0) {
                     for (int w2 = 0; w2 < NWARPS; ++w2) {
                         const Ent* sl = xl + w2 * SLOT;
@@ -231,14 +236,23 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
                     }
                 }
                 csync();
+                MXS_PROF_ADD(1, tof);
+                if (tid == 0) {
+                    int n_off = 0;
+                    for (int w2 = 0; w2 < NWARPS; ++w2) n_off += sm.warp_tot[w2];
+                    MXS_PROF_COUNT(4, n_off);
+                    MXS_PROF_COUNT(5, 1);
+                }
                 base += len;
                 size = min(2 * size, (int64_t)65536);
             }
         }
     }
+    MXS_PROF_T0(tsd);
     if (tid == 0) heap_sort(h, k);
     csync();
     block_draw(p, row, h, k, pbuf, sm);
+    MXS_PROF_ADD(2, tsd);
 }
 
 }  // namespace mxs

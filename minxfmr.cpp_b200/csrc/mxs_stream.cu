@@ -484,12 +484,29 @@ __global__ void __launch_bounds__(NT) exact_rows_kernel(Params p) {
     extern __shared__ __align__(128) unsigned char esmem[];
     Misc& sm = *reinterpret_cast<Misc*>(esmem + REGION_BYTES);
     const uint32_t n = *reinterpret_cast<volatile uint32_t*>(p.xcount);
+    MXS_PROF_BEGIN();
+    MXS_PROF_T0(tt);
     for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
         const int64_t row = p.xrows[i];
         const uint32_t f = p.row_flag[row];
         exact_row(p, row, (f & FLAG_NAN) ? 1 : 0, esmem, sm);
     }
+    MXS_PROF_ADD(7, tt);
+    MXS_PROF_FLUSH();
 }
+
+#ifdef MXS_PROFILE
+// Phase timers of the exact kernel: 0 filter, 1 offers, 2 sort+draw, 3 build,
+// 4 offers made (count), 5 steps (count), 7 total.
+extern "C" __attribute__((visibility("default"))) int mxs_prof_read_exact(unsigned long long* host, int clear) {
+    if (cudaMemcpyFromSymbol(host, g_mxs_prof, sizeof(g_mxs_prof)) != cudaSuccess) return -3;
+    if (clear) {
+        static unsigned long long zeros[PROF_CTAS][PROF_PHASES];
+        if (cudaMemcpyToSymbol(g_mxs_prof, zeros, sizeof(zeros)) != cudaSuccess) return -3;
+    }
+    return 0;
+}
+#endif
 
 size_t stream_smem_bytes() { return S_SMEM; }
 

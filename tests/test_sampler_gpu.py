@@ -94,7 +94,7 @@ def test_config5_throughput_shapes(mxs, rows):
     got = run_gpu(mxs, x, 0.8, 50, u)
     assert_parity(x, 0.8, 50, u, got, name=f"c5 rows={rows}")
     # tie-free N(0, 2^2) rows must stay on the streaming path, not the replay
-    assert ((got[3] & mxs.ROW_EXACT) != 0).mean() <= 0.01
+    assert ((got[3] & mxs.ROW_EXACT) != 0).sum() <= max(1, rows // 100)
 
 
 def test_ragged_vocab_strided_and_unaligned(mxs):
