@@ -34,8 +34,8 @@ __device__ __forceinline__ bool before(float a, float b) { return a > b; }
 
 // Heap over h[0, len) (generic pointer: shared or global memory). Serial: one
 // thread runs these.
-__device__ __forceinline__ void heap_sift_up(Ent* h, int64_t hole, int64_t top, Ent e) {
-    int64_t parent = (hole - 1) / 2;
+__device__ __forceinline__ void heap_sift_up(Ent* h, int hole, int top, Ent e) {
+    int parent = (hole - 1) / 2;
     while (hole > top && before(h[parent].v, e.v)) {
         h[hole] = h[parent];
         hole = parent;
@@ -44,10 +44,10 @@ __device__ __forceinline__ void heap_sift_up(Ent* h, int64_t hole, int64_t top, 
     h[hole] = e;
 }
 
-__device__ __forceinline__ void heap_place(Ent* h, int64_t hole, int64_t len, Ent e) {
-    const int64_t top = hole;
-    int64_t c = hole;
-    const int64_t inner = (len - 1) / 2;
+__device__ __forceinline__ void heap_place(Ent* h, int hole, int len, Ent e) {
+    const int top = hole;
+    int c = hole;
+    const int inner = (len - 1) / 2;
     while (c < inner) {
         c = 2 * (c + 1);
         const Ent r = h[c];
@@ -68,9 +68,9 @@ __device__ __forceinline__ void heap_place(Ent* h, int64_t hole, int64_t len, En
     heap_sift_up(h, hole, top, e);
 }
 
-__device__ __forceinline__ void heap_build(Ent* h, int64_t len) {
+__device__ __forceinline__ void heap_build(Ent* h, int len) {
     if (len < 2) return;
-    for (int64_t p = (len - 2) / 2;; --p) {
+    for (int p = (len - 2) / 2;; --p) {
         heap_place(h, p, len, h[p]);
         if (p == 0) break;
     }
@@ -78,12 +78,12 @@ __device__ __forceinline__ void heap_build(Ent* h, int64_t len) {
 
 // Offer entry e (index > every index already offered): replaces the root when
 // e's value is strictly greater than the root's.
-__device__ __forceinline__ void heap_offer(Ent* h, int64_t len, Ent e) {
+__device__ __forceinline__ void heap_offer(Ent* h, int len, Ent e) {
     if (before(e.v, h[0].v)) heap_place(h, 0, len, e);
 }
 
 // After this, h[0, len) is in the reference's top-k order (greatest first).
-__device__ __forceinline__ void heap_sort(Ent* h, int64_t len) {
+__device__ __forceinline__ void heap_sort(Ent* h, int len) {
     while (len > 1) {
         --len;
         const Ent e = h[len];

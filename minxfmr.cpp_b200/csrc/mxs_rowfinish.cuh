@@ -40,7 +40,7 @@ __device__ __forceinline__ double seq_sum(const double* p, int n) {
 
 // Top-p then min-p on the normalised probabilities pbuf[0, k), renormalising
 // in place as src/api/minxfmr.cpp:2128-2165 does; returns how many stay. Serial.
-__device__ inline int truncate_p(double* pbuf, int k, double top_p, double min_p) {
+__device__ __forceinline__ int truncate_p(double* pbuf, int k, double top_p, double min_p) {
     int n = k;
     if (top_p < 1.0) {  // src/api/minxfmr.cpp:2128-2145
         double cum = 0.0;
@@ -75,7 +75,7 @@ __device__ inline int truncate_p(double* pbuf, int k, double top_p, double min_p
 // Running partial sums of pbuf[0, n) in place, last forced to 1.0, then the
 // first index whose cumulative value is not below u (discrete_distribution's
 // _M_initialize + operator(), bits/random.tcc:2657-2714). Serial.
-__device__ inline int cdf_pick(double* pbuf, int n, double u) {
+__device__ __forceinline__ int cdf_pick(double* pbuf, int n, double u) {
     double run = 0.0;
     int i = 0;
     for (; i + 8 <= n; i += 8) {  // loads of a block of 8 issue together; the adds stay in order
@@ -101,7 +101,7 @@ __device__ inline int cdf_pick(double* pbuf, int n, double u) {
 // (bits/random.tcc:2657-2714): each double operation of the reference happens
 // here in the same order on the same operands. The k exps and the divisions are
 // independent and run across the CTA; the three running sums stay sequential.
-__device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, int k, double* pbuf, Misc& sm) {
+__device__ __forceinline__ void block_draw(const Params& p, int64_t row, const Ent* e, int k, double* pbuf, Misc& sm) {
     const int tid = threadIdx.x;
     if (p.topk_idx)
         for (int i = tid; i < k; i += NT) p.topk_idx[row * k + i] = e[i].i;
@@ -154,15 +154,18 @@ __device__ inline void block_draw(const Params& p, int64_t row, const Ent* e, in
 // -1 = unknown (scanned here). With a NaN anywhere the heap order is no longer
 // a total order, the root can shrink, and the lower-bound filter is not valid:
 // every element is then offered serially.
-__device__ inline void exact_row(const Params& p, int64_t row, int nan_state, unsigned char* region, Misc& sm) {
+template <bool SMALL>
+__device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int nan_state, unsigned char* region,
+                                            Misc& sm) {
     const int tid = threadIdx.x;
     const int k = p.k_use;
     const int64_t V = p.vocab;
     const float* x = p.logits + row * p.ld;
-    const bool small = (k <= HEAP_SMEM_MAX);
-    Ent* h = small ? reinterpret_cast<Ent*>(region) : p.heap_ws + (int64_t)blockIdx.x * k;
+    // SMALL: the heap lives in shared memory (k <= HEAP_SMEM_MAX); each case is
+    // its own instantiation so every heap access has a known address space.
+    Ent* h = SMALL ? reinterpret_cast<Ent*>(region) : p.heap_ws + (int64_t)blockIdx.x * k;
     Ent* xl = reinterpret_cast<Ent*>(region + HEAP_SMEM_MAX * sizeof(Ent));
-    double* pbuf = small ? reinterpret_cast<double*>(region + HEAP_SMEM_MAX * sizeof(Ent))
+    double* pbuf = SMALL ? reinterpret_cast<double*>(region + HEAP_SMEM_MAX * sizeof(Ent))
                          : p.prob_ws + (int64_t)blockIdx.x * k;
 
     if (nan_state < 0) {
@@ -253,6 +256,16 @@ __device__ inline void exact_row(const Params& p, int64_t row, int nan_state, un
     csync();
     block_draw(p, row, h, k, pbuf, sm);
     MXS_PROF_ADD(2, tsd);
+}
+
+// Exact replay of the reference's partial_sort heap process over row `row`,
+// then the draw (see exact_row_t).
+__device__ __forceinline__ void exact_row(const Params& p, int64_t row, int nan_state, unsigned char* region,
+                                          Misc& sm) {
+    if (p.k_use <= HEAP_SMEM_MAX)
+        exact_row_t<true>(p, row, nan_state, region, sm);
+    else
+        exact_row_t<false>(p, row, nan_state, region, sm);
 }
 
 }  // namespace mxs

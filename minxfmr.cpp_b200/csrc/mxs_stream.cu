@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
 }
 
 // One CTA per handed-over row (grid-stride over the list).
-__global__ void __launch_bounds__(NT) exact_rows_kernel(Params p) {
+__global__ void __launch_bounds__(NT, 1) exact_rows_kernel(Params p) {
     extern __shared__ __align__(128) unsigned char esmem[];
     Misc& sm = *reinterpret_cast<Misc*>(esmem + REGION_BYTES);
     const uint32_t n = *reinterpret_cast<volatile uint32_t*>(p.xcount);
