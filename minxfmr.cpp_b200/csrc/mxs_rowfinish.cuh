@@ -3,7 +3,6 @@
 #pragma once
 
 #include "mxs_sampler_kernel.cuh"
-#include "mxs_warp_heap.cuh"
 
 namespace mxs {
 
@@ -174,23 +173,10 @@ __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int na
         for (int64_t j = tid; j < V; j += NT) has |= (x[j] != x[j]);
         nan_state = csync_or(has) ? 1 : 0;
     }
-    // k <= 64 without NaNs: warp 0 keeps the heap in registers (mxs_warp_heap.cuh)
-    // and publishes the root's value in sm.thr for the filtering warps.
-    const bool wheap = SMALL && k <= WHEAP_MAX && nan_state == 0;
-    WarpHeap wh{0ull, 0ull};
     MXS_PROF_T0(tb);
     for (int i = tid; i < k; i += NT) h[i] = Ent{x[i], i};
     csync();
-    if (wheap) {
-        if (tid < 32) {
-            wh_load(wh, h, k);
-            wh_build(wh, k);
-            const uint64_t root = wh_get(wh, 0);
-            if (tid == 0) sm.thr = wh_val(root);
-        }
-    } else if (tid == 0) {
-        heap_build(h, k);
-    }
+    if (tid == 0) heap_build(h, k);
     csync();
     MXS_PROF_ADD(3, tb);
     if (k < V) {
@@ -218,7 +204,7 @@ __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int na
                 const int64_t seg = (len + NWARPS - 1) / NWARPS;
                 const int64_t lo = base + min((int64_t)w * seg, len);
                 const int64_t hi = base + min((int64_t)(w + 1) * seg, len);
-                const float r0 = wheap ? sm.thr : h[0].v;
+                const float r0 = h[0].v;
                 MXS_PROF_T0(tfl);
                 int c = 0;
                 for (int64_t g = lo; g < hi; g += 256) {
@@ -245,17 +231,7 @@ __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int na
                 }
                 MXS_PROF_ADD(0, tfl);
                 MXS_PROF_T0(tof);
-                if (wheap) {
-                    if (tid < 32) {
-                        for (int w2 = 0; w2 < NWARPS; ++w2) {
-                            const Ent* sl = xl + w2 * SLOT;
-                            const int n2 = sm.warp_tot[w2];
-                            for (int i = 0; i < n2; ++i) wh_offer(wh, k, wh_pack(sl[i].v, sl[i].i));
-                        }
-                        const uint64_t root = wh_get(wh, 0);
-                        if (tid == 0) sm.thr = wh_val(root);
-                    }
-                } else if (tid == 0) {
+                if (tid == 0) {
                     for (int w2 = 0; w2 < NWARPS; ++w2) {
                         const Ent* sl = xl + w2 * SLOT;
                         const int n2 = sm.warp_tot[w2];
@@ -276,14 +252,7 @@ __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int na
         }
     }
     MXS_PROF_T0(tsd);
-    if (wheap) {
-        if (tid < 32) {
-            wh_sort(wh, k);
-            wh_store(wh, h, k);
-        }
-    } else if (tid == 0) {
-        heap_sort(h, k);
-    }
+    if (tid == 0) heap_sort(h, k);
     csync();
     block_draw(p, row, h, k, pbuf, sm);
     MXS_PROF_ADD(2, tsd);
