@@ -353,7 +353,9 @@ struct FinishWarpSmem {
     Ent e[KSPLIT_K];
 };
 
-__device__ void warp_draw(const Params& p, int64_t row, const Ent* e, int k, double* pbuf) {
+// Draws for row `row` from e[0, k) and writes next (and the optional outputs);
+// returns the drawn position (in every lane).
+__device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, double* pbuf) {
     const int lane = threadIdx.x & 31;
     if (p.topk_idx)
         for (int i = lane; i < k; i += 32) p.topk_idx[row * k + i] = e[i].i;
@@ -372,7 +374,7 @@ __device__ void warp_draw(const Params& p, int64_t row, const Ent* e, int k, dou
         if (p.topk_prob)
             for (int i = lane; i < k; i += 32) p.topk_prob[row * k + i] = (i == 0) ? 1.0 : 0.0;
         if (lane == 0) p.next[row] = e[0].i;
-        return;
+        return 0;
     }
     for (int i = lane; i < k; i += 32) {
         const double q = pbuf[i] / sum;
@@ -391,11 +393,16 @@ __device__ void warp_draw(const Params& p, int64_t row, const Ent* e, int k, dou
     __syncwarp();
     if (n < 2) {  // discrete_distribution with fewer than two weights returns 0
         if (lane == 0) p.next[row] = e[0].i;
-        return;
+        return 0;
     }
     for (int i = lane; i < n; i += 32) pbuf[i] = pbuf[i] / s2;
     __syncwarp();
-    if (lane == 0) p.next[row] = e[cdf_pick(pbuf, n, p.u[row])].i;
+    int pick = 0;
+    if (lane == 0) {
+        pick = cdf_pick(pbuf, n, p.u[row]);
+        p.next[row] = e[pick].i;
+    }
+    return __shfl_sync(0xffffffffu, pick, 0);
 }
 
 __global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
@@ -442,29 +449,48 @@ __global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
                 }
             }
         }
+        // Ties among the survivors, or across the cut, make the reference's
+        // order of the equal values a product of its heap process. The
+        // probabilities and their running sums depend only on the values by
+        // position, so without a requested top-k list the draw is exact unless
+        // it lands on a tied position; only then does the row need the replay.
+        bool tie = false;
         if (!exact && cnt > k) {
             const uint32_t kth = warp_select_kth(w.keys, cnt, k, w.hist);
             cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
-            exact = (cnt != k);  // a tie straddles the cut
-        } else if (cnt < k) {
+            if (cnt != k) {  // a tie straddles the cut
+                tie = true;
+                exact = (cnt > KSPLIT_K) || (p.topk_idx != nullptr);
+            }
+        } else if (!exact && cnt < k) {
             exact = true;
         }
         if (!exact) {
-            uint64_t b0 = lane < k ? ((uint64_t)w.keys[lane] << 32) | (uint32_t)w.idx[lane] : 0ull;
-            uint64_t b1 = lane + 32 < k ? ((uint64_t)w.keys[lane + 32] << 32) | (uint32_t)w.idx[lane + 32] : 0ull;
+            uint64_t b0 = lane < cnt ? ((uint64_t)w.keys[lane] << 32) | (uint32_t)w.idx[lane] : 0ull;
+            uint64_t b1 = lane + 32 < cnt ? ((uint64_t)w.keys[lane + 32] << 32) | (uint32_t)w.idx[lane + 32] : 0ull;
             warp_sort64_desc(b0, b1);
             const uint64_t first1 = __shfl_sync(0xffffffffu, b1, 0);
+            const uint64_t last0 = __shfl_sync(0xffffffffu, b0, 31);
             const uint64_t dn0 = __shfl_down_sync(0xffffffffu, b0, 1);
-            const uint64_t n1 = __shfl_down_sync(0xffffffffu, b1, 1);
-            const uint64_t n0 = (lane == 31) ? first1 : dn0;
-            const bool tie = (lane < k - 1 && (b0 >> 32) == (n0 >> 32)) ||
-                             (lane + 32 < k - 1 && (b1 >> 32) == (n1 >> 32));
-            exact = __any_sync(0xffffffffu, tie);
+            const uint64_t dn1 = __shfl_down_sync(0xffffffffu, b1, 1);
+            const uint64_t up0 = __shfl_up_sync(0xffffffffu, b0, 1);
+            const uint64_t up1 = __shfl_up_sync(0xffffffffu, b1, 1);
+            const uint64_t n0 = (lane == 31) ? first1 : dn0;   // position lane + 1
+            const uint64_t pr1 = (lane == 0) ? last0 : up1;     // position lane + 31
+            // tied[i]: position i < k holds a value equal to a neighbour among the cnt sorted
+            const bool t0 = lane < k && ((lane > 0 && (b0 >> 32) == (up0 >> 32)) ||
+                                         (lane + 1 < cnt && (b0 >> 32) == (n0 >> 32)));
+            const bool t1 = lane + 32 < k && (((b1 >> 32) == (pr1 >> 32)) ||
+                                              (lane + 33 < cnt && (b1 >> 32) == (dn1 >> 32)));
+            const uint32_t tm0 = __ballot_sync(0xffffffffu, t0), tm1 = __ballot_sync(0xffffffffu, t1);
+            tie = tie || (tm0 | tm1) != 0u;
+            if (tie && p.topk_idx) exact = true;
             if (!exact) {
                 if (lane < k) w.e[lane] = Ent{fkey_inv((uint32_t)(b0 >> 32)), (int32_t)(uint32_t)b0};
                 if (lane + 32 < k) w.e[lane + 32] = Ent{fkey_inv((uint32_t)(b1 >> 32)), (int32_t)(uint32_t)b1};
                 __syncwarp();
-                warp_draw(p, row, w.e, k, w.pbuf);
+                const int pick = warp_draw(p, row, w.e, k, w.pbuf);
+                if (tie && (((pick < 32 ? tm0 : tm1) >> (pick & 31)) & 1u)) exact = true;
             }
         }
     }
