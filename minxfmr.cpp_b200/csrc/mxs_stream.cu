@@ -158,8 +158,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
     uint32_t* wk = wkeys + warp * SW_CAP;
     int32_t* wi = widx + warp * SW_CAP;
     uint32_t* whist = whist_all + warp * 256;
-    const int m = (k + NWARPS - 1) / NWARPS;
-    const int wtrig = max(2 * m, 32);
+    const int m = (k + NWARPS - 1) / NWARPS;  // <= 8
     uint32_t cseq = 0;
     bool dead = false;  // a wait ran out: stop waiting, flag every later row
     for (int64_t j = 0; j < nj; ++j) {
@@ -169,10 +168,29 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
         const int nt = unit_tiles(u);
         const float* xr = p.logits + row * p.ld;
         UnitState& us = sm.us[j % SLOTS];
-        int wcnt = 0, nan = 0, ntrig = wtrig;
+        int wcnt = 0, nan = 0;
         uint32_t fl = dead ? FLAG_TIMEOUT : 0u;
         bool stopped = false;
         float wseed = -INFINITY;  // this warp's own bound from its first tile
+        // Lanes 0..m-1: the m largest keys this warp has held, descending
+        // (0 = none yet). Its m-th is what the warp publishes (see stream_shrink).
+        uint32_t lkey = 0u, mypub = 0u;
+        auto publish = [&]() {
+            const uint32_t km = __shfl_sync(0xffffffffu, lkey, m - 1);
+            if (km > mypub) {
+                mypub = km;
+                if (lane == 0) atomicMax(&us.pub[warp], km);
+                __syncwarp();
+                uint32_t mn = (lane < NWARPS) ? *reinterpret_cast<volatile uint32_t*>(&us.pub[lane]) : 0xFFFFFFFFu;
+#pragma unroll
+                for (int d = 16; d > 0; d >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, d));
+                if (lane == 0 && mn) atomicMax(&us.thr_key, mn);
+            }
+        };
+        auto bound = [&]() -> float {
+            const float b = bound_of(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
+            return b > wseed ? b : wseed;
+        };
         for (int t = 0; t < nt; ++t, ++cseq) {
             const int64_t a = ((int64_t)c * TPC + t) * TILE;
             const int len = (int)(min(a + TILE, V) - a);
@@ -214,8 +232,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 // Seeds from the unit's first tile. Per lane: the largest and
                 // second largest logit (64 distinct logits per warp).
                 //  - own bound: the k-th largest of those 64 (k <= 64 logits are >= it);
-                //  - published: the m-th largest lane maximum, m = ceil(k / NWARPS);
-                //    the smallest over all warps bounds the unit (see stream_shrink).
+                //  - top-m list: the m largest lane maxima (m distinct logits).
                 float m1 = -INFINITY, m2 = -INFINITY;
 #pragma unroll
                 for (int b = 0; b < 16; ++b) {
@@ -235,17 +252,11 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 warp_sort64_desc(s0, s1);
                 const uint64_t kth = (k <= 32) ? __shfl_sync(0xffffffffu, s0, k - 1) : __shfl_sync(0xffffffffu, s1, k - 33);
                 wseed = bound_of((uint32_t)(kth >> 32));
-                const uint32_t km = warp_sort32_desc((nv >= 1) ? fkey(m1) : 0u);
-                const uint32_t pm = __shfl_sync(0xffffffffu, km, m - 1);
-                if (lane == 0 && pm) atomicMax(&us.pub[warp], pm);
-                __syncwarp();
-                uint32_t mn = (lane < NWARPS) ? *reinterpret_cast<volatile uint32_t*>(&us.pub[lane]) : 0xFFFFFFFFu;
-#pragma unroll
-                for (int d = 16; d > 0; d >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, d));
-                if (lane == 0 && mn) atomicMax(&us.thr_key, mn);
+                lkey = (uint32_t)(s0 >> 32);  // lane i: the (i+1)-th largest of the 64 (distinct logits)
+                if (lane >= m) lkey = 0u;
+                publish();
             }
-            float thr = bound_of(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
-            thr = thr > wseed ? thr : wseed;
+            const float thr = bound();
             if (!stopped && __any_sync(0xffffffffu, mxn >= thr)) {
                 auto pass_bits = [&](float th) -> uint32_t {
                     uint32_t mm = 0;
@@ -261,37 +272,22 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 int incl = warp_incl_scan(cc);
                 int tot = __shfl_sync(0xffffffffu, incl, 31);
                 if (wcnt + tot > SW_CAP) {
-                    // Does not fit (no bound yet, or a loose one): take the
-                    // four float4 groups one at a time, shrinking in between.
-                    for (int q = 0; q < 4 && !stopped; ++q) {
-                        stream_shrink(wk, wi, wcnt, k, whist, us);
-                        float th = bound_of(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
-                        th = th > wseed ? th : wseed;
-                        uint32_t mq = (pass_bits(th) >> (4 * q)) & 0xFu;
-                        const int cq = __popc(mq);
-                        const int iq = warp_incl_scan(cq);
-                        const int tq = __shfl_sync(0xffffffffu, iq, 31);
-                        if (wcnt + tq > SW_CAP) {  // massive ties: the exact replay takes the row
-                            stopped = true;
-                            fl |= FLAG_OVERFLOW;
-                            break;
-                        }
-                        int pq = wcnt + iq - cq;
-                        while (mq) {
-                            const int b = 4 * q + __ffs(mq) - 1;
-                            mq &= mq - 1;
-                            const int e = 4 * (warp * 128 + lane + 32 * q) + (b & 3);
-                            const float v = (e < bulk_n) ? st[e] : xr[a + e];
-                            wk[pq] = fkey(v);
-                            wi[pq] = (int32_t)(a + e);
-                            ++pq;
-                        }
-                        wcnt += tq;
+                    // Make room: drop what the shared bound excludes; if that is
+                    // not enough, select (stream_shrink); filter the tile again.
+                    wcnt = warp_compact_ge(wk, wi, wcnt, *reinterpret_cast<volatile uint32_t*>(&us.thr_key));
+                    if (wcnt + tot > SW_CAP) stream_shrink(wk, wi, wcnt, k, whist, us);
+                    mm = pass_bits(bound());
+                    cc = __popc(mm);
+                    incl = warp_incl_scan(cc);
+                    tot = __shfl_sync(0xffffffffu, incl, 31);
+                    if (wcnt + tot > SW_CAP) {  // massive ties: the exact replay takes the row
+                        stopped = true;
+                        fl |= FLAG_OVERFLOW;
+                        mm = 0;
+                        cc = 0;
+                        incl = 0;
+                        tot = 0;
                     }
-                    mm = 0;
-                    cc = 0;
-                    incl = 0;
-                    tot = 0;
                 }
                 int pos = wcnt + incl - cc;
                 while (mm) {
@@ -303,12 +299,24 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     wi[pos] = (int32_t)(a + e);
                     ++pos;
                 }
-                wcnt += tot;
-                if (wcnt > ntrig) {
-                    stream_shrink(wk, wi, wcnt, k, whist, us);
-                    ntrig = min(SW_CAP - 64, max(wtrig, 2 * wcnt));
+                __syncwarp();
+                // Fold the new keys into the top-m list: lanes m..31 take up to
+                // 32 - m of them per round, one register sort keeps the m largest.
+                // Not on the first tile: its logits seeded the list already, and
+                // counting a logit twice would break the bound's guarantee.
+                for (int r0 = 0; t > 0 && r0 < tot; r0 += 32 - m) {
+                    const int ii = r0 + lane - m;
+                    uint32_t v = lkey;
+                    if (lane >= m) v = (ii < tot) ? wk[wcnt + ii] : 0u;
+                    v = warp_sort32_desc(v);
+                    lkey = (lane < m) ? v : 0u;
                 }
+                wcnt += tot;
+                if (tot && t > 0) publish();
+                if (wcnt > SW_CAP - 64)
+                    wcnt = warp_compact_ge(wk, wi, wcnt, *reinterpret_cast<volatile uint32_t*>(&us.thr_key));
             }
+            // every lane of the warp is done with the stage: hand it back
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.empty[s])) : "memory");
         }
