@@ -159,7 +159,8 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
     int32_t* wi = widx + warp * SW_CAP;
     uint32_t* whist = whist_all + warp * 256;
     const int m = (k + NWARPS - 1) / NWARPS;  // <= 8
-    uint32_t cseq = 0;
+    int s = 0;             // ring stage of the next tile
+    uint32_t parity = 0;   // its phase parity
     bool dead = false;  // a wait ran out: stop waiting, flag every later row
     for (int64_t j = 0; j < nj; ++j) {
         const int64_t u = blockIdx.x + j * G;
@@ -191,12 +192,13 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             const float b = bound_of(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
             return b > wseed ? b : wseed;
         };
-        for (int t = 0; t < nt; ++t, ++cseq) {
-            const int64_t a = ((int64_t)c * TPC + t) * TILE;
-            const int len = (int)(min(a + TILE, V) - a);
+        const int a0 = c * TPC * TILE;  // the unit's first column (V < 2^31)
+        const int last_len = (int)(V - (int64_t)(a0 + (nt - 1) * TILE));
+        for (int t = 0; t < nt; ++t) {
+            const int a = a0 + t * TILE;
+            const int len = (t == nt - 1) ? last_len : TILE;
             const int bulk_n = len & ~3;
-            const int s = cseq % STAGES;
-            if (!dead && !mbar_wait_bounded(&sm.full[s], (cseq / STAGES) & 1)) {
+            if (!dead && !mbar_wait_bounded(&sm.full[s], parity)) {
                 fl |= FLAG_TIMEOUT;
                 dead = true;
             }
@@ -304,12 +306,23 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 // 32 - m of them per round, one register sort keeps the m largest.
                 // Not on the first tile: its logits seeded the list already, and
                 // counting a logit twice would break the bound's guarantee.
-                for (int r0 = 0; t > 0 && r0 < tot; r0 += 32 - m) {
-                    const int ii = r0 + lane - m;
-                    uint32_t v = lkey;
-                    if (lane >= m) v = (ii < tot) ? wk[wcnt + ii] : 0u;
-                    v = warp_sort32_desc(v);
-                    lkey = (lane < m) ? v : 0u;
+                if (t > 0 && tot <= 4) {
+                    // a few keys: insert each one by rank (ballot) and a shift
+                    for (int ii = 0; ii < tot; ++ii) {
+                        const uint32_t v = wk[wcnt + ii];
+                        const uint32_t above = __ballot_sync(0xffffffffu, lane < m && lkey >= v);
+                        const int r = __popc(above);  // lanes 0..r-1 keep their keys
+                        const uint32_t up = __shfl_up_sync(0xffffffffu, lkey, 1);
+                        if (r < m && lane >= r && lane < m) lkey = (lane == r) ? v : up;
+                    }
+                } else {
+                    for (int r0 = 0; t > 0 && r0 < tot; r0 += 32 - m) {
+                        const int ii = r0 + lane - m;
+                        uint32_t v = lkey;
+                        if (lane >= m) v = (ii < tot) ? wk[wcnt + ii] : 0u;
+                        v = warp_sort32_desc(v);
+                        lkey = (lane < m) ? v : 0u;
+                    }
                 }
                 wcnt += tot;
                 if (tot && t > 0) publish();
@@ -319,6 +332,10 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             // every lane of the warp is done with the stage: hand it back
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.empty[s])) : "memory");
+            if (++s == STAGES) {
+                s = 0;
+                parity ^= 1u;
+            }
         }
         // Leave the unit: append the survivors (>= the bound now) to the row's list.
         const uint32_t T = *reinterpret_cast<volatile uint32_t*>(&us.thr_key);
