@@ -32,9 +32,12 @@ TOP_K = 50
 SIGMA = 2.0
 METRIC = "sampled rows/s (V=151936 fp32, top_k 50)"
 UNIT = "rows/s"
-# ncu dram__bytes_read.sum + dram__bytes_write.sum of one sample_kernel launch
-# per row of this workload (profiles/sample_kernel_b4096_v151936.md); None until captured.
-NCU_TRAFFIC_BYTES_PER_ROW = None
+# ncu dram__bytes_read.sum + dram__bytes_write.sum of one stream_select_kernel
+# launch per row of this workload, from a 512-row capture of the same kernel
+# (profiles/stream_select_kernel_c5.md): 311,246,336 + 3,920,640 bytes / 512 rows.
+# Traffic grows in proportion to the rows, so it is scaled to a full launch.
+NCU_TRAFFIC_BYTES_PER_ROW = (311246336 + 3920640) / 512
+DOMINANT_KERNEL = "mxs::stream_select_kernel"
 
 
 def env_rank():
@@ -199,6 +202,11 @@ def main():
     torch.cuda.synchronize()
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    # device timing of the dominant kernel in every timed step (library hook)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, b in kev:  # torch creates the CUDA events on their first record
+        a.record(stream)
+        b.record(stream)
     with ClockSampler(gpu_index) as clk:
         if world > 1:
             dist.barrier()
@@ -206,10 +214,13 @@ def main():
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            mxs_sampler.set_profile_events(*kev[i])
             step()
         ev1.record(stream)
         torch.cuda.synchronize()
+        mxs_sampler.set_profile_events(None, None)
+        kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
         if world > 1:
             dist.barrier()
         ms_total = ev0.elapsed_time(ev1)
@@ -250,11 +261,14 @@ def main():
     if rank == 0:
         peak, peak_kind = peaks()
         bytes_per_launch = rows * V * 4
-        achieved = bytes_per_launch / (ms_total / args.steps / 1e3) / 1e9
+        achieved = bytes_per_launch / (kernel_ms / 1e3) / 1e9
+        step_gbs = bytes_per_launch / (ms_total / args.steps / 1e3) / 1e9
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                    "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs (burst copy)",
+                    "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs (burst copy), of measured",
                     "traffic": (NCU_TRAFFIC_BYTES_PER_ROW * rows) if NCU_TRAFFIC_BYTES_PER_ROW else None,
-                    "kernel": "mxs::sample_kernel<true>", "algorithmic_bytes_per_launch": bytes_per_launch}
+                    "kernel": DOMINANT_KERNEL, "kernel_ms": kernel_ms,
+                    "algorithmic_bytes_per_launch": bytes_per_launch,
+                    "whole_step_gbs": step_gbs, "whole_step_frac": step_gbs / peak}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             v, kind, cores, desc = cpu_reference_run(256, args.cpu_seconds)
@@ -266,7 +280,7 @@ def main():
                                        "one uniform per row", "rows_per_gpu": rows, "vocab": V, "top_k": TOP_K,
                            "temperature": TEMPERATURE, "parallelism": f"row-sharded x{world}, no collective",
                            "l2": "inputs (2.49 GB per GPU) larger than L2; no flush"},
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 3 * args.steps,
                 "hbm_frac_of_8tbs": achieved / 8000.0, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -136,6 +136,16 @@ MXS_API int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count
                      double* d_topk_prob, uint32_t* d_row_flags, void* stream);
 
 /*
+ * Measurement hook (no counterpart in the reference): when set, the next
+ * sampling calls on the current device record `start` and `stop` (cudaEvent_t,
+ * created by the caller) on the call's stream immediately around the launch of
+ * the row-streaming kernel, the call's dominant kernel, so its duration can be
+ * timed on the device apart from the short finishing kernels. NULL, NULL
+ * turns it off.
+ */
+MXS_API int mxs_set_profile_events(void* start, void* stop);
+
+/*
  * No counterpart in the reference: an addition of this library for callers that
  * cannot allocate device memory (hosts whose memory pool owns the whole GPU, or
  * that forbid allocation on the per-token path). Same arguments and results as

@@ -34,6 +34,7 @@ struct Device {
     int sms = 0;
     int blocks_per_sm = 0;
     void* ws = nullptr;  // library-owned workspace (zeroed at allocation)
+    cudaEvent_t ev_start = nullptr, ev_stop = nullptr;  // mxs_set_profile_events
     size_t ws_bytes = 0;
     HostBuffers hb;
 };
@@ -205,21 +206,24 @@ void clamp_p(double* top_p, double* min_p) {  // src/api/minxfmr.cpp:2109-2111
     if (*min_p > 1.0) *min_p = 1.0;
 }
 
-int launch(Params& p, const Plan& pl, cudaStream_t stream, int sms = 148) {
+int launch(Params& p, const Plan& pl, cudaStream_t stream, int sms = 148, cudaEvent_t ev0 = nullptr,
+           cudaEvent_t ev1 = nullptr) {
     p.S = pl.S;
     p.tiles_per_chunk = pl.tpc;
     p.units = pl.units;
     p.outcap = pl.outcap;
     if (pl.split) {
         if (cudaMemsetAsync(p.row_cnt, 0, pl.zero_bytes, stream) != cudaSuccess) return MXS_ERR_CUDA;
-        if (mxs::stream_path_launch(p, pl.grid, sms, stream) != cudaSuccess) return MXS_ERR_CUDA;
+        if (mxs::stream_path_launch(p, pl.grid, sms, stream, ev0, ev1) != cudaSuccess) return MXS_ERR_CUDA;
         return MXS_OK;
     }
     const bool tma = (reinterpret_cast<uintptr_t>(p.logits) % 16 == 0) && (p.ld % 4 == 0);
     // MXS_SAMPLER_BLOCK_PATH=1 selects the CTA-synchronous streaming kernel for
     // every k (the parity tests run both kernels).
     p.force_block_path = path_override() == 2 ? 1 : 0;
+    if (ev0) cudaEventRecord(ev0, stream);
     if (mxs::sample_kernel_launch(p, pl.grid, tma, stream) != cudaSuccess) return MXS_ERR_CUDA;
+    if (ev1) cudaEventRecord(ev1, stream);
     return MXS_OK;
 }
 
@@ -290,7 +294,7 @@ int mxs_sample_topk_ex(const float* d_logits, int64_t rows, int64_t vocab, int64
     p.row_flags = d_row_flags;
     p.mode = mxs::MODE_SAMPLE;
     fill_workspace(p, pl, ws);
-    return launch(p, pl, (cudaStream_t)stream, d->sms);
+    return launch(p, pl, (cudaStream_t)stream, d->sms, d->ev_start, d->ev_stop);
 }
 
 int mxs_sample_topk(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
@@ -436,6 +440,17 @@ int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count_all, co
     p.units = pl.units;
     p.outcap = 0;
     if (mxs::sample_kernel_launch(p, pl.grid, false, (cudaStream_t)stream) != cudaSuccess) return MXS_ERR_CUDA;
+    return MXS_OK;
+}
+
+int mxs_set_profile_events(void* start, void* stop) {
+    if ((start == nullptr) != (stop == nullptr)) return MXS_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Device* d;
+    int rc = current_device(&d);
+    if (rc) return rc;
+    d->ev_start = (cudaEvent_t)start;
+    d->ev_stop = (cudaEvent_t)stop;
     return MXS_OK;
 }
 

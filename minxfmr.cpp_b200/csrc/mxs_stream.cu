@@ -573,9 +573,12 @@ cudaError_t stream_path_configure(int* blocks_per_sm) {
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, stream_select_kernel, NT_WS, S_SMEM);
 }
 
-cudaError_t stream_path_launch(const Params& p, int grid, int exact_grid, cudaStream_t stream) {
+cudaError_t stream_path_launch(const Params& p, int grid, int exact_grid, cudaStream_t stream, cudaEvent_t ev_start,
+                               cudaEvent_t ev_stop) {
+    if (ev_start) cudaEventRecord(ev_start, stream);
     stream_select_kernel<<<grid, NT_WS, S_SMEM, stream>>>(p);
     cudaError_t e = cudaGetLastError();
+    if (ev_stop) cudaEventRecord(ev_stop, stream);
     if (e != cudaSuccess) return e;
     finish_rows_kernel<<<(unsigned)((p.rows + F_WARPS - 1) / F_WARPS), F_WARPS * 32, sizeof(FinishWarpSmem) * F_WARPS,
                          stream>>>(p);

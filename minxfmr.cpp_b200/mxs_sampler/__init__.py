@@ -36,7 +36,7 @@ ROW_TIMEOUT = 8
 EXPORTS = (
     "mxs_sample_topk", "mxs_sample_topk_ex", "mxs_workspace_size", "mxs_workspace_init",
     "mxs_sample_topk_host", "mxs_shard_candidates", "mxs_merge_sample", "mxs_get_status",
-    "mxs_version", "mxs_sample_topk_noalloc",
+    "mxs_version", "mxs_sample_topk_noalloc", "mxs_set_profile_events",
 )
 
 _P = ctypes.c_void_p
@@ -54,6 +54,7 @@ _SIGS = {
     "mxs_shard_candidates": [_P, _I64, _I64, _I64, _I64, _I, _I, _P, _P, _P, _P],
     "mxs_merge_sample": [_P, _P, _P, _I, _I, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _P],
     "mxs_get_status": [ctypes.POINTER(ctypes.c_uint32), _I],
+    "mxs_set_profile_events": [_P, _P],
     "mxs_sample_topk_noalloc": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _P],
 }
 
@@ -253,6 +254,14 @@ def merge_sample(cand_all, count_all, flags_all, vocab, temperature, top_k, u, t
                                      _ptr(prob), _ptr(rflg), _stream(stream))
     _check("mxs_merge_sample", rc)
     return nxt, idx, prob, rflg
+
+
+def set_profile_events(start=None, stop=None):
+    """Record torch.cuda.Event pair around the dominant (row-streaming) kernel of
+    the next calls on the current device; None, None turns it off."""
+    sp = None if start is None else ctypes.c_void_p(start.cuda_event)
+    ep = None if stop is None else ctypes.c_void_p(stop.cuda_event)
+    _check("mxs_set_profile_events", load().mxs_set_profile_events(sp, ep))
 
 
 def get_status(clear=True):
