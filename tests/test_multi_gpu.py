@@ -1,0 +1,85 @@
+"""Multi-GPU tests (NCCL, one process per GPU; skipped with fewer than 2 GPUs).
+
+- vocab-sharded sampling: each rank holds one column shard; candidate lists are
+  all-gathered and merged on every rank; the result must equal the oracle's on
+  the full rows, on every rank, tie rows included;
+- row-sharded bench: bench.py under torchrun prints one JSON line."""
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+WORKER = r'''
+import os, sys, json, numpy as np, torch, torch.distributed as dist
+sys.path.insert(0, os.path.join(os.environ["ROOT"], "minxfmr.cpp_b200"))
+sys.path.insert(0, os.path.join(os.environ["ROOT"], "tests"))
+rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+import workloads, oracle_lib
+from mxs_sampler.dist import VocabShardedSampler
+rows, V, k, T = 64, 151936, 50, 0.8
+x = workloads.normal(77, rows, V, 2.0)
+x[3, 1000:1040] = 9.5           # tie row inside one shard
+x[5, [10, V - 10]] = 11.0       # tie across shards
+u = oracle_lib.uniforms(77, rows)
+cols = V // world
+shard = torch.from_numpy(x[:, rank * cols:(rank + 1) * cols].copy()).cuda()
+vs = VocabShardedSampler(V)
+nxt, idx, prob, fl = vs.sample(shard, T, k, torch.from_numpy(u).cuda())
+torch.cuda.synchronize()
+n0, i0, p0 = oracle_lib.oracle_sample(x, T, k, u)
+ok = bool((nxt.cpu().numpy() == n0).all() and (idx.cpu().numpy() == i0).all()
+          and np.allclose(prob.cpu().numpy(), p0, rtol=1e-6, atol=0))
+print(json.dumps({"rank": rank, "ok": ok, "exact_rows": int((fl.cpu().numpy() & 1).sum())}), flush=True)
+dist.destroy_process_group()
+sys.exit(0 if ok else 3)
+'''
+
+
+def _need_gpus(n):
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+
+
+def test_vocab_sharded_nccl_two_gpus():
+    _need_gpus(2)
+    port = _free_port()
+    env = dict(os.environ, ROOT=ROOT, MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE="2",
+               NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, "-c", WORKER], env=dict(env, RANK=str(r), LOCAL_RANK=str(r)),
+                              stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True) for r in range(2)]
+    outs = [p.communicate(timeout=600)[0] for p in procs]
+    for p, o in zip(procs, outs):
+        assert p.returncode == 0, o[-3000:]
+        line = [l for l in o.splitlines() if l.startswith("{")][-1]
+        d = json.loads(line)
+        assert d["ok"] and d["exact_rows"] >= 2
+
+
+def test_row_sharded_bench_two_gpus():
+    _need_gpus(2)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
+           "127.0.0.1", "--master-port", str(_free_port()), os.path.join(ROOT, "bench.py"), "--gpus", "2", "--steps",
+           "20", "--warmup", "3", "--no-e2e"]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-3000:]
+    line = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
+    assert line["n_gpus"] == 2 and line["value"] > 0 and line["cpu_baseline"] is None
