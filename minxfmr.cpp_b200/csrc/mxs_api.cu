@@ -111,7 +111,8 @@ Plan make_plan(const Device& d, int64_t rows, int64_t vocab, int k_use, bool mer
     pl.k_use = k_use;
     pl.split = split;
     const int64_t full = (int64_t)d.sms * d.blocks_per_sm;
-    const int64_t ntl = (vocab + mxs::TILE - 1) / mxs::TILE;
+    const int tile = split ? mxs::S_TILE : mxs::TILE;  // logits per ring stage of the chosen kernel
+    const int64_t ntl = (vocab + tile - 1) / tile;
     if (merge_mode || k_use > mxs::KFAST) {
         pl.S = 1;
         pl.tpc = (int)ntl;

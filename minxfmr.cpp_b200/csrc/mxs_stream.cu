@@ -34,12 +34,12 @@ struct UnitState {
 };
 
 struct StreamSmem {
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
+    uint64_t full[S_STAGES];
+    uint64_t empty[S_STAGES];
     UnitState us[SLOTS];
 };
 
-constexpr size_t S_RING = size_t(STAGES) * TILE * 4;
+constexpr size_t S_RING = size_t(S_STAGES) * S_TILE * 4;
 constexpr size_t S_WBUF = size_t(NWARPS) * SW_CAP * 8;
 constexpr size_t S_HIST = size_t(NWARPS) * 256 * 4;
 constexpr size_t S_SMEM = S_RING + S_WBUF + S_HIST + sizeof(StreamSmem);
@@ -106,14 +106,14 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
     const int64_t G = gridDim.x;
     const int64_t nj = (p.units > (int64_t)blockIdx.x) ? (p.units - blockIdx.x + G - 1) / G : 0;
     const int S = p.S, TPC = p.tiles_per_chunk;
-    const int64_t NTL = (V + TILE - 1) / TILE;
+    const int64_t NTL = (V + S_TILE - 1) / S_TILE;
     auto unit_tiles = [&](int64_t u) -> int {
         const int64_t t0 = (int64_t)(u % S) * TPC;
         return (int)min((int64_t)TPC, NTL - t0);
     };
 
     if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < S_STAGES; ++s) {
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], NWARPS);
         }
@@ -135,17 +135,17 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 const int64_t row = u / S;
                 const int nt = unit_tiles(u);
                 for (int t = 0; t < nt; ++t, ++seq) {
-                    const int s = seq % STAGES;
-                    if (seq >= STAGES && !mbar_wait_bounded(&sm.empty[s], ((seq / STAGES) - 1) & 1)) {
+                    const int s = seq % S_STAGES;
+                    if (seq >= S_STAGES && !mbar_wait_bounded(&sm.empty[s], ((seq / S_STAGES) - 1) & 1)) {
                         atomicOr(&p.row_flag[row], FLAG_TIMEOUT);
                         return;  // consumers time out on the stages that never come
                     }
-                    const int64_t a = ((int64_t)(u % S) * TPC + t) * TILE;
-                    const int64_t b = min(a + TILE, V);
+                    const int64_t a = ((int64_t)(u % S) * TPC + t) * S_TILE;
+                    const int64_t b = min(a + S_TILE, V);
                     const uint32_t bytes = (uint32_t)(((b - a) & ~int64_t(3)) * 4);
                     if (bytes) {
                         mbar_arrive_expect_tx(&sm.full[s], bytes);
-                        bulk_g2s(ring + s * TILE, p.logits + row * p.ld + a, bytes, &sm.full[s], pol);
+                        bulk_g2s(ring + s * S_TILE, p.logits + row * p.ld + a, bytes, &sm.full[s], pol);
                     } else {
                         asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.full[s])) : "memory");
                     }
@@ -192,30 +192,30 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             const float b = bound_of(*reinterpret_cast<volatile uint32_t*>(&us.thr_key));
             return b > wseed ? b : wseed;
         };
-        const int a0 = c * TPC * TILE;  // the unit's first column (V < 2^31)
-        const int last_len = (int)(V - (int64_t)(a0 + (nt - 1) * TILE));
+        const int a0 = c * TPC * S_TILE;  // the unit's first column (V < 2^31)
+        const int last_len = (int)(V - (int64_t)(a0 + (nt - 1) * S_TILE));
         for (int t = 0; t < nt; ++t) {
-            const int a = a0 + t * TILE;
-            const int len = (t == nt - 1) ? last_len : TILE;
+            const int a = a0 + t * S_TILE;
+            const int len = (t == nt - 1) ? last_len : S_TILE;
             const int bulk_n = len & ~3;
             if (!dead && !mbar_wait_bounded(&sm.full[s], parity)) {
                 fl |= FLAG_TIMEOUT;
                 dead = true;
             }
-            const float* st = ring + s * TILE;
-            float vv[16];
-            uint32_t valid = 0xFFFFu;
-            if (len == TILE) {
+            const float* st = ring + s * S_TILE;
+            float vv[32];
+            uint32_t valid = 0xFFFFFFFFu;
+            if (len == S_TILE) {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 f = *reinterpret_cast<const float4*>(st + 4 * (warp * 128 + lane + 32 * q));
+                for (int q = 0; q < 8; ++q) {
+                    const float4 f = *reinterpret_cast<const float4*>(st + 4 * (warp * 256 + lane + 32 * q));
                     vv[4 * q] = f.x; vv[4 * q + 1] = f.y; vv[4 * q + 2] = f.z; vv[4 * q + 3] = f.w;
                 }
             } else {
                 valid = 0;
 #pragma unroll
-                for (int b = 0; b < 16; ++b) {
-                    const int e = 4 * (warp * 128 + lane + 32 * (b >> 2)) + (b & 3);
+                for (int b = 0; b < 32; ++b) {
+                    const int e = 4 * (warp * 256 + lane + 32 * (b >> 2)) + (b & 3);
                     vv[b] = -INFINITY;
                     if (e < len) {
                         vv[b] = (e < bulk_n) ? st[e] : xr[a + e];
@@ -223,21 +223,23 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     }
                 }
             }
-            float mx8[8];
+            float mx16[16];
 #pragma unroll
-            for (int b = 0; b < 8; ++b) mx8[b] = fmax_nan(vv[2 * b], vv[2 * b + 1]);
+            for (int b = 0; b < 16; ++b) mx16[b] = fmax_nan(vv[2 * b], vv[2 * b + 1]);
 #pragma unroll
-            for (int b = 0; b < 4; ++b) mx8[b] = fmax_nan(mx8[2 * b], mx8[2 * b + 1]);
-            const float mxn = fmax_nan(fmax_nan(mx8[0], mx8[1]), fmax_nan(mx8[2], mx8[3]));
+            for (int b = 0; b < 8; ++b) mx16[b] = fmax_nan(mx16[2 * b], mx16[2 * b + 1]);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) mx16[b] = fmax_nan(mx16[2 * b], mx16[2 * b + 1]);
+            const float mxn = fmax_nan(fmax_nan(mx16[0], mx16[1]), fmax_nan(mx16[2], mx16[3]));
             nan |= (mxn != mxn);
             if (t == 0) {
                 // Seeds from the unit's first tile. Per lane: the largest and
-                // second largest logit (64 distinct logits per warp).
+                // second largest of its 32 logits (64 distinct logits per warp).
                 //  - own bound: the k-th largest of those 64 (k <= 64 logits are >= it);
                 //  - top-m list: the m largest lane maxima (m distinct logits).
                 float m1 = -INFINITY, m2 = -INFINITY;
 #pragma unroll
-                for (int b = 0; b < 16; ++b) {
+                for (int b = 0; b < 32; ++b) {
                     if ((valid >> b) & 1u) {
                         const float x = vv[b];
                         if (x > m1) {
@@ -264,7 +266,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     uint32_t mm = 0;
                     if (mxn >= th) {
 #pragma unroll
-                        for (int b = 0; b < 16; ++b)
+                        for (int b = 0; b < 32; ++b)
                             if (vv[b] >= th) mm |= 1u << b;
                     }
                     return mm & valid;
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 while (mm) {
                     const int b = __ffs(mm) - 1;
                     mm &= mm - 1;
-                    const int e = 4 * (warp * 128 + lane + 32 * (b >> 2)) + (b & 3);
+                    const int e = 4 * (warp * 256 + lane + 32 * (b >> 2)) + (b & 3);
                     const float v = (e < bulk_n) ? st[e] : xr[a + e];
                     wk[pos] = fkey(v);
                     wi[pos] = (int32_t)(a + e);
@@ -332,7 +334,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             // every lane of the warp is done with the stage: hand it back
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.empty[s])) : "memory");
-            if (++s == STAGES) {
+            if (++s == S_STAGES) {
                 s = 0;
                 parity ^= 1u;
             }
@@ -352,7 +354,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
         if (__any_sync(0xffffffffu, nan)) fl |= FLAG_NAN;
         if (lane == 0 && fl) atomicOr(&p.row_flag[row], fl);
         // The last warp out recycles the slot for unit j + SLOTS (no warp can be
-        // that far ahead: the ring keeps them within STAGES tiles of each other).
+        // that far ahead: the ring keeps them within S_STAGES tiles of each other).
         __syncwarp();
         if (lane == 0) {
             __threadfence_block();
