@@ -70,8 +70,7 @@ struct Plan {
     int k_use = 1;
     int S = 1, tpc = 1, grid = 1, outcap = 0;
     bool split = false;  // three-kernel path (stream -> finish -> exact)
-    size_t off_rcand = 0, off_rcnt = 0, off_rflag = 0, off_runits = 0, off_xcount = 0, off_xrows = 0,
-           zero_bytes = 0;
+    size_t off_rcand = 0, off_rcnt = 0, off_rflag = 0, off_xcount = 0, off_xrows = 0, zero_bytes = 0;
     int64_t units = 0;
     size_t off_counter = 0, off_state = 0, off_status = 0, off_ccount = 0, off_cand = 0, off_heap = 0,
            off_prob = 0, total = 0;
@@ -145,8 +144,7 @@ Plan make_plan(const Device& d, int64_t rows, int64_t vocab, int k_use, bool mer
         // per-row counters, flags and the exact-row count: cleared by every call
         pl.off_rcnt = o;
         pl.off_rflag = pl.off_rcnt + sizeof(uint32_t) * (size_t)rows;
-        pl.off_runits = pl.off_rflag + sizeof(uint32_t) * (size_t)rows;
-        pl.off_xcount = pl.off_runits + sizeof(uint32_t) * (size_t)rows;
+        pl.off_xcount = pl.off_rflag + sizeof(uint32_t) * (size_t)rows;
         pl.zero_bytes = pl.off_xcount + 16 - pl.off_rcnt;
         o = align_up(pl.off_xcount + 16, 256);
         pl.off_xrows = o;
@@ -197,7 +195,6 @@ void fill_workspace(Params& p, const Plan& pl, void* ws) {
         p.row_cand = reinterpret_cast<uint64_t*>(b + pl.off_rcand);
         p.row_cnt = reinterpret_cast<uint32_t*>(b + pl.off_rcnt);
         p.row_flag = reinterpret_cast<uint32_t*>(b + pl.off_rflag);
-        p.row_units = reinterpret_cast<uint32_t*>(b + pl.off_runits);
         p.row_cap = split_row_cap(pl.S);
         p.xcount = reinterpret_cast<uint32_t*>(b + pl.off_xcount);
         p.xrows = reinterpret_cast<int32_t*>(b + pl.off_xrows);

@@ -77,7 +77,6 @@ struct Params {
     uint32_t* row_cnt;         // rows: entries appended (may exceed row_cap: overflow)
     uint32_t* row_flag;        // rows: OR of FLAG_* seen while streaming
     int row_cap;
-    uint32_t* row_units;       // rows: units (chunks) of the row finished so far
     uint32_t* xcount;          // rows handed to the exact kernel
     int32_t* xrows;            // rows: their indices
 };

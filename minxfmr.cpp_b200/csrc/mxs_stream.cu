@@ -1,16 +1,15 @@
-// Two-kernel sampling path for k <= KSPLIT on 16-byte aligned rows.
+// Three-kernel sampling path for k <= KSPLIT on 16-byte aligned rows.
 //
 //  1. stream_select_kernel: a producer warp streams every tile of the CTA's
 //     (row, chunk) units through a bulk-copy ring; 8 consumer warps each filter
-//     a 1024-logit slice of every tile against a shared lower bound of the
+//     a 512-logit slice of every tile against a shared lower bound of the
 //     unit's k-th largest value, with no CTA-wide barrier at all: per-unit
 //     state lives in an 8-slot ring recycled by the last warp to leave a unit,
 //     and each warp appends its surviving candidates to the row's list in
 //     global memory when it leaves the unit.
-//  2. a finisher warp in the same CTA (finish_row_warp), per row as soon as
-//     its units are done: selects the k-th largest candidate,
+//  2. finish_rows_kernel: one warp per row selects the k-th largest candidate,
 //     sorts the k survivors in registers, checks for ties and draws.
-//  3. exact_rows_kernel: one CTA per row the finisher handed over (a tie,
+//  3. exact_rows_kernel: one CTA per row the finish kernel handed over (a tie,
 //     a NaN, an overflow) replays the reference's heap process over the row.
 #include <cmath>
 #include <cstdint>
@@ -38,22 +37,12 @@ struct StreamSmem {
     uint64_t full[S_STAGES];
     uint64_t empty[S_STAGES];
     UnitState us[SLOTS];
-    uint32_t units_done;  // units of this CTA every consumer warp has left
-};
-
-struct FinishWarpSmem {
-    uint32_t keys[FCAP];
-    int32_t idx[FCAP];
-    uint32_t hist[256];
-    double pbuf[KSPLIT_K];
-    Ent e[KSPLIT_K];
 };
 
 constexpr size_t S_RING = size_t(S_STAGES) * S_TILE * 4;
 constexpr size_t S_WBUF = size_t(NWARPS) * SW_CAP * 8;
 constexpr size_t S_HIST = size_t(NWARPS) * 256 * 4;
-constexpr size_t S_FIN = (S_RING + S_WBUF + S_HIST + sizeof(StreamSmem) + 15) / 16 * 16;  // finisher's area
-constexpr size_t S_SMEM = S_FIN + sizeof(FinishWarpSmem);
+constexpr size_t S_SMEM = S_RING + S_WBUF + S_HIST + sizeof(StreamSmem);
 
 // Publish this warp's m-th largest key; the smallest value every warp has
 // published bounds the unit's k-th largest from below (the warps' slices are
@@ -103,161 +92,7 @@ __device__ __forceinline__ uint32_t warp_sort32_desc(uint32_t v) {
     return v;
 }
 
-// One warp per row: select, register sort, tie check, draw; rows that need the
-// exact replay go to the exact kernel's list.
-
-// Draws for row `row` from e[0, k) and writes next (and the optional outputs);
-// returns the drawn position (in every lane).
-__device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, double* pbuf) {
-    const int lane = threadIdx.x & 31;
-    if (p.topk_idx)
-        for (int i = lane; i < k; i += 32) p.topk_idx[row * k + i] = e[i].i;
-    const double T = p.temperature;
-    bool greedy = (T <= 0.0);
-    double sum = 0.0;
-    if (!greedy) {
-        const double maxs = (double)e[0].v;
-        for (int i = lane; i < k; i += 32) pbuf[i] = exp(((double)e[i].v - maxs) / T);
-        __syncwarp();
-        if (lane == 0) sum = seq_sum(pbuf, k);
-        sum = __shfl_sync(0xffffffffu, sum, 0);
-        greedy = (sum <= 0.0);
-    }
-    if (greedy) {
-        if (p.topk_prob)
-            for (int i = lane; i < k; i += 32) p.topk_prob[row * k + i] = (i == 0) ? 1.0 : 0.0;
-        if (lane == 0) p.next[row] = e[0].i;
-        return 0;
-    }
-    for (int i = lane; i < k; i += 32) {
-        const double q = pbuf[i] / sum;
-        pbuf[i] = q;
-        if (p.topk_prob) p.topk_prob[row * k + i] = q;
-    }
-    __syncwarp();
-    int n = 0;
-    double s2 = 0.0;
-    if (lane == 0) {
-        n = truncate_p(pbuf, k, p.top_p, p.min_p);
-        s2 = (n >= 2) ? seq_sum(pbuf, n) : 0.0;
-    }
-    n = __shfl_sync(0xffffffffu, n, 0);
-    s2 = __shfl_sync(0xffffffffu, s2, 0);
-    __syncwarp();
-    if (n < 2) {  // discrete_distribution with fewer than two weights returns 0
-        if (lane == 0) p.next[row] = e[0].i;
-        return 0;
-    }
-    for (int i = lane; i < n; i += 32) pbuf[i] = pbuf[i] / s2;
-    __syncwarp();
-    int pick = 0;
-    if (lane == 0) {
-        pick = cdf_pick(pbuf, n, p.u[row]);
-        p.next[row] = e[pick].i;
-    }
-    return __shfl_sync(0xffffffffu, pick, 0);
-}
-
-// Finish row `row` with one warp: its candidate list (written by the
-// streaming warps, possibly of other CTAs) is read with L2-coherent loads.
-__device__ void finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w) {
-    const int lane = threadIdx.x & 31;
-    const int k = p.k_use;
-    uint32_t flags = __ldcg(p.row_flag + row);
-    const uint32_t cnt_all = __ldcg(p.row_cnt + row);
-    bool exact = (flags & (FLAG_NAN | FLAG_OVERFLOW)) != 0 || cnt_all > (uint32_t)p.row_cap ||
-                 cnt_all < (uint32_t)k;
-    if (!(flags & FLAG_TIMEOUT) && !exact) {
-        // Take the list in batches of 32 against a running bound (the k-th
-        // largest key held once the buffer has filled), so lists longer than
-        // the buffer (a row split over many chunks) still fit.
-        const uint64_t* src = p.row_cand + row * (int64_t)p.row_cap;
-        const uint32_t lt = (1u << lane) - 1u;
-        int cnt = 0;
-        uint32_t bound = 0u;
-        for (int i0 = 0; i0 < (int)cnt_all; i0 += 32) {
-            const int i = i0 + lane;
-            uint64_t v = 0;
-            bool take = false;
-            if (i < (int)cnt_all) {
-                v = __ldcg(src + i);
-                take = (uint32_t)(v >> 32) >= bound;
-            }
-            const uint32_t bal = __ballot_sync(0xffffffffu, take);
-            if (take) {
-                const int pos = cnt + __popc(bal & lt);
-                w.keys[pos] = (uint32_t)(v >> 32);
-                w.idx[pos] = (int32_t)(uint32_t)v;
-            }
-            cnt += __popc(bal);
-            __syncwarp();
-            if (cnt > FCAP - 32) {
-                bound = warp_select_kth(w.keys, cnt, k, w.hist);
-                cnt = warp_compact_ge(w.keys, w.idx, cnt, bound);
-                if (cnt > FCAP - 32) {  // massive ties
-                    exact = true;
-                    break;
-                }
-            }
-        }
-        // Ties among the survivors, or across the cut, make the reference's
-        // order of the equal values a product of its heap process. The
-        // probabilities and their running sums depend only on the values by
-        // position, so without a requested top-k list the draw is exact unless
-        // it lands on a tied position; only then does the row need the replay.
-        bool tie = false;
-        if (!exact && cnt > k) {
-            const uint32_t kth = warp_select_kth(w.keys, cnt, k, w.hist);
-            cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
-            if (cnt != k) {  // a tie straddles the cut
-                tie = true;
-                exact = (cnt > KSPLIT_K) || (p.topk_idx != nullptr);
-            }
-        } else if (!exact && cnt < k) {
-            exact = true;
-        }
-        if (!exact) {
-            uint64_t b0 = lane < cnt ? ((uint64_t)w.keys[lane] << 32) | (uint32_t)w.idx[lane] : 0ull;
-            uint64_t b1 = lane + 32 < cnt ? ((uint64_t)w.keys[lane + 32] << 32) | (uint32_t)w.idx[lane + 32] : 0ull;
-            warp_sort64_desc(b0, b1);
-            const uint64_t first1 = __shfl_sync(0xffffffffu, b1, 0);
-            const uint64_t last0 = __shfl_sync(0xffffffffu, b0, 31);
-            const uint64_t dn0 = __shfl_down_sync(0xffffffffu, b0, 1);
-            const uint64_t dn1 = __shfl_down_sync(0xffffffffu, b1, 1);
-            const uint64_t up0 = __shfl_up_sync(0xffffffffu, b0, 1);
-            const uint64_t up1 = __shfl_up_sync(0xffffffffu, b1, 1);
-            const uint64_t n0 = (lane == 31) ? first1 : dn0;   // position lane + 1
-            const uint64_t pr1 = (lane == 0) ? last0 : up1;     // position lane + 31
-            // tied[i]: position i < k holds a value equal to a neighbour among the cnt sorted
-            const bool t0 = lane < k && ((lane > 0 && (b0 >> 32) == (up0 >> 32)) ||
-                                         (lane + 1 < cnt && (b0 >> 32) == (n0 >> 32)));
-            const bool t1 = lane + 32 < k && (((b1 >> 32) == (pr1 >> 32)) ||
-                                              (lane + 33 < cnt && (b1 >> 32) == (dn1 >> 32)));
-            const uint32_t tm0 = __ballot_sync(0xffffffffu, t0), tm1 = __ballot_sync(0xffffffffu, t1);
-            tie = tie || (tm0 | tm1) != 0u;
-            if (tie && p.topk_idx) exact = true;
-            if (!exact) {
-                if (lane < k) w.e[lane] = Ent{fkey_inv((uint32_t)(b0 >> 32)), (int32_t)(uint32_t)b0};
-                if (lane + 32 < k) w.e[lane + 32] = Ent{fkey_inv((uint32_t)(b1 >> 32)), (int32_t)(uint32_t)b1};
-                __syncwarp();
-                const int pick = warp_draw(p, row, w.e, k, w.pbuf);
-                if (tie && (((pick < 32 ? tm0 : tm1) >> (pick & 31)) & 1u)) exact = true;
-            }
-        }
-    }
-    if (lane == 0) {
-        if (flags & FLAG_TIMEOUT) {
-            p.next[row] = -1;
-            atomicOr(p.status, flags);
-        } else if (exact) {
-            p.xrows[atomicAdd(p.xcount, 1u)] = (int32_t)row;
-        }
-        if (p.row_flags) p.row_flags[row] = flags | ((exact && !(flags & FLAG_TIMEOUT)) ? FLAG_EXACT : 0u);
-    }
-}
-
-
-__global__ void __launch_bounds__(NT_WS + 32, 2) stream_select_kernel(Params p) {
+__global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
     extern __shared__ __align__(128) unsigned char smem[];
     float* ring = reinterpret_cast<float*>(smem);
     uint32_t* wkeys = reinterpret_cast<uint32_t*>(smem + S_RING);
@@ -282,7 +117,6 @@ __global__ void __launch_bounds__(NT_WS + 32, 2) stream_select_kernel(Params p) 
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], NWARPS);
         }
-        sm.units_done = 0u;
         for (int i = 0; i < SLOTS; ++i) {
             sm.us[i].thr_key = 0u;
             sm.us[i].done = 0u;
@@ -291,37 +125,6 @@ __global__ void __launch_bounds__(NT_WS + 32, 2) stream_select_kernel(Params p) 
         fence_mbar_init();
     }
     __syncthreads();
-
-    if (warp == NWARPS + 1) {  // finisher: one row at a time as its units complete
-        FinishWarpSmem& fw = *reinterpret_cast<FinishWarpSmem*>(smem + S_FIN);
-        for (int64_t j = 0; j < nj; ++j) {
-            // wait (bounded, ~1 s) until every consumer warp has left unit j
-            bool ok = *reinterpret_cast<volatile uint32_t*>(&sm.units_done) > (uint32_t)j;
-            if (!ok) {
-                const uint64_t t0 = globaltimer_ns();
-                while (!(ok = *reinterpret_cast<volatile uint32_t*>(&sm.units_done) > (uint32_t)j)) {
-                    if (globaltimer_ns() - t0 > 1000000000ull) break;
-                    __nanosleep(256);
-                }
-            }
-            const int64_t u = blockIdx.x + j * G;
-            const int64_t row = u / S;
-            if (!ok) {  // the consumers are stuck: flag this row; the later ones flag themselves
-                if (lane == 0) atomicOr(&p.row_flag[row], FLAG_TIMEOUT);
-                __syncwarp();
-            }
-            __threadfence();
-            bool mine = true;
-            if (S > 1) {  // the CTA that completes the row's last unit finishes it
-                uint32_t old = 0;
-                if (lane == 0) old = atomicAdd(&p.row_units[row], 1u);
-                mine = __shfl_sync(0xffffffffu, old, 0) == (uint32_t)(S - 1);
-                __threadfence();
-            }
-            if (mine) finish_row_warp(p, row, fw);
-        }
-        return;
-    }
 
     if (warp == NWARPS) {  // producer
         if (lane == 0) {
@@ -554,16 +357,178 @@ __global__ void __launch_bounds__(NT_WS + 32, 2) stream_select_kernel(Params p) 
         // that far ahead: the ring keeps them within S_STAGES tiles of each other).
         __syncwarp();
         if (lane == 0) {
-            __threadfence();  // the list entries are visible GPU-wide before the unit counts as left
+            __threadfence_block();
             if (atomicAdd(&us.done, 1u) == NWARPS - 1) {
                 us.thr_key = 0u;
                 for (int w = 0; w < NWARPS; ++w) us.pub[w] = 0u;
                 __threadfence_block();
                 us.done = 0u;
-                atomicAdd(&sm.units_done, 1u);  // hand the unit to the finisher
             }
         }
         __syncwarp();
+    }
+}
+
+// One warp per row: select, register sort, tie check, draw; rows that need the
+// exact replay go to the exact kernel's list.
+constexpr int F_WARPS = 8;
+struct FinishWarpSmem {
+    uint32_t keys[FCAP];
+    int32_t idx[FCAP];
+    uint32_t hist[256];
+    double pbuf[KSPLIT_K];
+    Ent e[KSPLIT_K];
+};
+
+// Draws for row `row` from e[0, k) and writes next (and the optional outputs);
+// returns the drawn position (in every lane).
+__device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, double* pbuf) {
+    const int lane = threadIdx.x & 31;
+    if (p.topk_idx)
+        for (int i = lane; i < k; i += 32) p.topk_idx[row * k + i] = e[i].i;
+    const double T = p.temperature;
+    bool greedy = (T <= 0.0);
+    double sum = 0.0;
+    if (!greedy) {
+        const double maxs = (double)e[0].v;
+        for (int i = lane; i < k; i += 32) pbuf[i] = exp(((double)e[i].v - maxs) / T);
+        __syncwarp();
+        if (lane == 0) sum = seq_sum(pbuf, k);
+        sum = __shfl_sync(0xffffffffu, sum, 0);
+        greedy = (sum <= 0.0);
+    }
+    if (greedy) {
+        if (p.topk_prob)
+            for (int i = lane; i < k; i += 32) p.topk_prob[row * k + i] = (i == 0) ? 1.0 : 0.0;
+        if (lane == 0) p.next[row] = e[0].i;
+        return 0;
+    }
+    for (int i = lane; i < k; i += 32) {
+        const double q = pbuf[i] / sum;
+        pbuf[i] = q;
+        if (p.topk_prob) p.topk_prob[row * k + i] = q;
+    }
+    __syncwarp();
+    int n = 0;
+    double s2 = 0.0;
+    if (lane == 0) {
+        n = truncate_p(pbuf, k, p.top_p, p.min_p);
+        s2 = (n >= 2) ? seq_sum(pbuf, n) : 0.0;
+    }
+    n = __shfl_sync(0xffffffffu, n, 0);
+    s2 = __shfl_sync(0xffffffffu, s2, 0);
+    __syncwarp();
+    if (n < 2) {  // discrete_distribution with fewer than two weights returns 0
+        if (lane == 0) p.next[row] = e[0].i;
+        return 0;
+    }
+    for (int i = lane; i < n; i += 32) pbuf[i] = pbuf[i] / s2;
+    __syncwarp();
+    int pick = 0;
+    if (lane == 0) {
+        pick = cdf_pick(pbuf, n, p.u[row]);
+        p.next[row] = e[pick].i;
+    }
+    return __shfl_sync(0xffffffffu, pick, 0);
+}
+
+__global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
+    extern __shared__ __align__(16) unsigned char fsmem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    FinishWarpSmem& w = reinterpret_cast<FinishWarpSmem*>(fsmem)[warp];
+    const int64_t row = (int64_t)blockIdx.x * F_WARPS + warp;
+    if (row >= p.rows) return;
+    const int k = p.k_use;
+    uint32_t flags = p.row_flag[row];
+    const uint32_t cnt_all = p.row_cnt[row];
+    bool exact = (flags & (FLAG_NAN | FLAG_OVERFLOW)) != 0 || cnt_all > (uint32_t)p.row_cap ||
+                 cnt_all < (uint32_t)k;
+    if (!(flags & FLAG_TIMEOUT) && !exact) {
+        // Take the list in batches of 32 against a running bound (the k-th
+        // largest key held once the buffer has filled), so lists longer than
+        // the buffer (a row split over many chunks) still fit.
+        const uint64_t* src = p.row_cand + row * (int64_t)p.row_cap;
+        const uint32_t lt = (1u << lane) - 1u;
+        int cnt = 0;
+        uint32_t bound = 0u;
+        for (int i0 = 0; i0 < (int)cnt_all; i0 += 32) {
+            const int i = i0 + lane;
+            uint64_t v = 0;
+            bool take = false;
+            if (i < (int)cnt_all) {
+                v = src[i];
+                take = (uint32_t)(v >> 32) >= bound;
+            }
+            const uint32_t bal = __ballot_sync(0xffffffffu, take);
+            if (take) {
+                const int pos = cnt + __popc(bal & lt);
+                w.keys[pos] = (uint32_t)(v >> 32);
+                w.idx[pos] = (int32_t)(uint32_t)v;
+            }
+            cnt += __popc(bal);
+            __syncwarp();
+            if (cnt > FCAP - 32) {
+                bound = warp_select_kth(w.keys, cnt, k, w.hist);
+                cnt = warp_compact_ge(w.keys, w.idx, cnt, bound);
+                if (cnt > FCAP - 32) {  // massive ties
+                    exact = true;
+                    break;
+                }
+            }
+        }
+        // Ties among the survivors, or across the cut, make the reference's
+        // order of the equal values a product of its heap process. The
+        // probabilities and their running sums depend only on the values by
+        // position, so without a requested top-k list the draw is exact unless
+        // it lands on a tied position; only then does the row need the replay.
+        bool tie = false;
+        if (!exact && cnt > k) {
+            const uint32_t kth = warp_select_kth(w.keys, cnt, k, w.hist);
+            cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
+            if (cnt != k) {  // a tie straddles the cut
+                tie = true;
+                exact = (cnt > KSPLIT_K) || (p.topk_idx != nullptr);
+            }
+        } else if (!exact && cnt < k) {
+            exact = true;
+        }
+        if (!exact) {
+            uint64_t b0 = lane < cnt ? ((uint64_t)w.keys[lane] << 32) | (uint32_t)w.idx[lane] : 0ull;
+            uint64_t b1 = lane + 32 < cnt ? ((uint64_t)w.keys[lane + 32] << 32) | (uint32_t)w.idx[lane + 32] : 0ull;
+            warp_sort64_desc(b0, b1);
+            const uint64_t first1 = __shfl_sync(0xffffffffu, b1, 0);
+            const uint64_t last0 = __shfl_sync(0xffffffffu, b0, 31);
+            const uint64_t dn0 = __shfl_down_sync(0xffffffffu, b0, 1);
+            const uint64_t dn1 = __shfl_down_sync(0xffffffffu, b1, 1);
+            const uint64_t up0 = __shfl_up_sync(0xffffffffu, b0, 1);
+            const uint64_t up1 = __shfl_up_sync(0xffffffffu, b1, 1);
+            const uint64_t n0 = (lane == 31) ? first1 : dn0;   // position lane + 1
+            const uint64_t pr1 = (lane == 0) ? last0 : up1;     // position lane + 31
+            // tied[i]: position i < k holds a value equal to a neighbour among the cnt sorted
+            const bool t0 = lane < k && ((lane > 0 && (b0 >> 32) == (up0 >> 32)) ||
+                                         (lane + 1 < cnt && (b0 >> 32) == (n0 >> 32)));
+            const bool t1 = lane + 32 < k && (((b1 >> 32) == (pr1 >> 32)) ||
+                                              (lane + 33 < cnt && (b1 >> 32) == (dn1 >> 32)));
+            const uint32_t tm0 = __ballot_sync(0xffffffffu, t0), tm1 = __ballot_sync(0xffffffffu, t1);
+            tie = tie || (tm0 | tm1) != 0u;
+            if (tie && p.topk_idx) exact = true;
+            if (!exact) {
+                if (lane < k) w.e[lane] = Ent{fkey_inv((uint32_t)(b0 >> 32)), (int32_t)(uint32_t)b0};
+                if (lane + 32 < k) w.e[lane + 32] = Ent{fkey_inv((uint32_t)(b1 >> 32)), (int32_t)(uint32_t)b1};
+                __syncwarp();
+                const int pick = warp_draw(p, row, w.e, k, w.pbuf);
+                if (tie && (((pick < 32 ? tm0 : tm1) >> (pick & 31)) & 1u)) exact = true;
+            }
+        }
+    }
+    if (lane == 0) {
+        if (flags & FLAG_TIMEOUT) {
+            p.next[row] = -1;
+            atomicOr(p.status, flags);
+        } else if (exact) {
+            p.xrows[atomicAdd(p.xcount, 1u)] = (int32_t)row;
+        }
+        if (p.row_flags) p.row_flags[row] = flags | ((exact && !(flags & FLAG_TIMEOUT)) ? FLAG_EXACT : 0u);
     }
 }
 
@@ -601,18 +566,25 @@ size_t stream_smem_bytes() { return S_SMEM; }
 cudaError_t stream_path_configure(int* blocks_per_sm) {
     cudaError_t e = cudaFuncSetAttribute(stream_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(finish_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(FinishWarpSmem) * F_WARPS));
+    if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(exact_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)(REGION_BYTES + sizeof(Misc)));
     if (e != cudaSuccess) return e;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, stream_select_kernel, NT_WS + 32, S_SMEM);
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, stream_select_kernel, NT_WS, S_SMEM);
 }
 
 cudaError_t stream_path_launch(const Params& p, int grid, int exact_grid, cudaStream_t stream, cudaEvent_t ev_start,
                                cudaEvent_t ev_stop) {
     if (ev_start) cudaEventRecord(ev_start, stream);
-    stream_select_kernel<<<grid, NT_WS + 32, S_SMEM, stream>>>(p);
+    stream_select_kernel<<<grid, NT_WS, S_SMEM, stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (ev_stop) cudaEventRecord(ev_stop, stream);
+    if (e != cudaSuccess) return e;
+    finish_rows_kernel<<<(unsigned)((p.rows + F_WARPS - 1) / F_WARPS), F_WARPS * 32, sizeof(FinishWarpSmem) * F_WARPS,
+                         stream>>>(p);
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     exact_rows_kernel<<<exact_grid, NT, REGION_BYTES + sizeof(Misc), stream>>>(p);
     return cudaGetLastError();
