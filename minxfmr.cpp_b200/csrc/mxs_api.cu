@@ -214,6 +214,10 @@ int launch(Params& p, const Plan& pl, cudaStream_t stream, int sms = 148, cudaEv
     p.units = pl.units;
     p.outcap = pl.outcap;
     if (pl.split) {
+        // MXS_DEBUG_DROP_TILE=n (tests only): CTA 0's producer stops before its
+        // n-th tile, so its consumers' bounded wait runs out (MXS_ROW_TIMEOUT).
+        const char* dt = getenv("MXS_DEBUG_DROP_TILE");
+        p.debug_drop_tile = dt ? atoll(dt) : -1;
         if (cudaMemsetAsync(p.row_cnt, 0, pl.zero_bytes, stream) != cudaSuccess) return MXS_ERR_CUDA;
         if (mxs::stream_path_launch(p, pl.grid, sms, stream, ev0, ev1) != cudaSuccess) return MXS_ERR_CUDA;
         return MXS_OK;

@@ -78,6 +78,8 @@ struct Params {
     uint32_t* row_flag;        // rows: OR of FLAG_* seen while streaming
     int row_cap;
     uint32_t* xcount;          // rows handed to the exact kernel
+    int64_t debug_drop_tile;   // test hook (MXS_DEBUG_DROP_TILE): the streaming producer stops before
+                               // the CTA-0 tile with this sequence number; -1 = off
     int32_t* xrows;            // rows: their indices
 };
 constexpr int MODE_SAMPLE = 0;

@@ -136,6 +136,10 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 const int nt = unit_tiles(u);
                 for (int t = 0; t < nt; ++t, ++seq) {
                     const int s = seq % S_STAGES;
+                    // Test hook: stop issuing (every earlier copy has been
+                    // waited for by the consumers, so none is left in flight);
+                    // the consumers' bounded wait then runs out.
+                    if (blockIdx.x == 0 && (int64_t)seq == p.debug_drop_tile) return;
                     if (seq >= S_STAGES && !mbar_wait_bounded(&sm.empty[s], ((seq / S_STAGES) - 1) & 1)) {
                         atomicOr(&p.row_flag[row], FLAG_TIMEOUT);
                         return;  // consumers time out on the stages that never come
