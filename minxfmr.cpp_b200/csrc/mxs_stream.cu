@@ -227,20 +227,19 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     }
                 }
             }
-            float mx16[16];
+            // max.NaN tree; oct[o] = max of values 8o..8o+7 (kept to screen octets)
+            float mx16[16], oct[4];
 #pragma unroll
             for (int b = 0; b < 16; ++b) mx16[b] = fmax_nan(vv[2 * b], vv[2 * b + 1]);
 #pragma unroll
             for (int b = 0; b < 8; ++b) mx16[b] = fmax_nan(mx16[2 * b], mx16[2 * b + 1]);
 #pragma unroll
-            for (int b = 0; b < 4; ++b) mx16[b] = fmax_nan(mx16[2 * b], mx16[2 * b + 1]);
-            const float mxn = fmax_nan(fmax_nan(mx16[0], mx16[1]), fmax_nan(mx16[2], mx16[3]));
+            for (int b = 0; b < 4; ++b) oct[b] = fmax_nan(mx16[2 * b], mx16[2 * b + 1]);
+            const float mxn = fmax_nan(fmax_nan(oct[0], oct[1]), fmax_nan(oct[2], oct[3]));
             nan |= (mxn != mxn);
             if (t == 0) {
-                // Seeds from the unit's first tile. Per lane: the largest and
-                // second largest of its 32 logits (64 distinct logits per warp).
-                //  - own bound: the k-th largest of those 64 (k <= 64 logits are >= it);
-                //  - top-m list: the m largest lane maxima (m distinct logits).
+                // Seeds from the unit's first tile, from each lane's largest and
+                // second largest logit (all distinct logits of the slice).
                 float m1 = -INFINITY, m2 = -INFINITY;
 #pragma unroll
                 for (int b = 0; b < 32; ++b) {
@@ -255,13 +254,20 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     }
                 }
                 const int nv = __popc(valid);
-                uint64_t s0 = (nv >= 1) ? (uint64_t)fkey(m1) << 32 : 0ull;
-                uint64_t s1 = (nv >= 2) ? (uint64_t)fkey(m2) << 32 : 0ull;
-                warp_sort64_desc(s0, s1);
-                const uint64_t kth = (k <= 32) ? __shfl_sync(0xffffffffu, s0, k - 1) : __shfl_sync(0xffffffffu, s1, k - 33);
-                wseed = bound_of((uint32_t)(kth >> 32));
-                lkey = (uint32_t)(s0 >> 32);  // lane i: the (i+1)-th largest of the 64 (distinct logits)
-                if (lane >= m) lkey = 0u;
+                // lane maxima sorted: lanes 0..m-1 seed the top-m list; for
+                // k <= 32 the k-th is also this warp's own bound (k distinct
+                // logits are >= it). For k > 32: the ceil(k/2)-th largest lane
+                // second-maximum (each of those lanes holds two logits >= it).
+                const uint32_t sorted1 = warp_sort32_desc(nv >= 1 ? fkey(m1) : 0u);
+                uint32_t own;
+                if (k <= 32) {
+                    own = __shfl_sync(0xffffffffu, sorted1, k - 1);
+                } else {
+                    const uint32_t sorted2 = warp_sort32_desc(nv >= 2 ? fkey(m2) : 0u);
+                    own = __shfl_sync(0xffffffffu, sorted2, (k + 1) / 2 - 1);
+                }
+                wseed = bound_of(own);
+                lkey = (lane < m) ? sorted1 : 0u;
                 publish();
             }
             const float thr = bound();
@@ -270,8 +276,13 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     uint32_t mm = 0;
                     if (mxn >= th) {
 #pragma unroll
-                        for (int b = 0; b < 32; ++b)
-                            if (vv[b] >= th) mm |= 1u << b;
+                        for (int o = 0; o < 4; ++o) {
+                            if (oct[o] >= th) {  // only octets whose maximum passes
+#pragma unroll
+                                for (int b = 8 * o; b < 8 * o + 8; ++b)
+                                    if (vv[b] >= th) mm |= 1u << b;
+                            }
+                        }
                     }
                     return mm & valid;
                 };
