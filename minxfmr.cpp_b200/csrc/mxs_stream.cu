@@ -23,7 +23,7 @@ namespace mxs {
 constexpr int KSPLIT_K = 64;        // largest k of this path (register sort of 64)
 constexpr int SW_CAP = 256;         // candidates per consumer warp
 constexpr int SLOTS = 8;            // per-unit state ring (> the STAGES a warp can run ahead)
-constexpr int FCAP = 1024;          // candidates per row the finish warp takes
+constexpr int FCAP = 256;           // candidate buffer of a finish warp (longer lists stream through it)
 static_assert(KSPLIT_K == KSPLIT, "KSPLIT must match the register sort");
 
 
