@@ -288,8 +288,15 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 };
                 uint32_t mm = pass_bits(thr);
                 int cc = __popc(mm);
-                int incl = warp_incl_scan(cc);
-                int tot = __shfl_sync(0xffffffffu, incl, 31);
+                int incl, tot;
+                if (!__any_sync(0xffffffffu, cc > 1)) {  // usual case: at most one per lane
+                    const uint32_t one = __ballot_sync(0xffffffffu, cc != 0);
+                    incl = __popc(one & ((2u << lane) - 1u));
+                    tot = __popc(one);
+                } else {
+                    incl = warp_incl_scan(cc);
+                    tot = __shfl_sync(0xffffffffu, incl, 31);
+                }
                 if (wcnt + tot > SW_CAP) {
                     // Make room: drop what the shared bound excludes; if that is
                     // not enough, select (stream_shrink); filter the tile again.
@@ -309,21 +316,29 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     }
                 }
                 int pos = wcnt + incl - cc;
+                // the warp's own m-th key: a new key below it cannot change the top-m list
+                const uint32_t own_mth = __shfl_sync(0xffffffffu, lkey, m - 1);
+                bool grows = false;
                 while (mm) {
                     const int b = __ffs(mm) - 1;
                     mm &= mm - 1;
                     const int e = 4 * (warp * 256 + lane + 32 * (b >> 2)) + (b & 3);
                     const float v = (e < bulk_n) ? st[e] : xr[a + e];
-                    wk[pos] = fkey(v);
+                    const uint32_t key = fkey(v);
+                    grows |= key > own_mth;
+                    wk[pos] = key;
                     wi[pos] = (int32_t)(a + e);
                     ++pos;
                 }
                 __syncwarp();
+                grows = __any_sync(0xffffffffu, grows);
                 // Fold the new keys into the top-m list: lanes m..31 take up to
                 // 32 - m of them per round, one register sort keeps the m largest.
                 // Not on the first tile: its logits seeded the list already, and
                 // counting a logit twice would break the bound's guarantee.
-                if (t > 0 && tot <= 4) {
+                if (!grows) {
+                    // nothing above the warp's own m-th: the list stays
+                } else if (t > 0 && tot <= 4) {
                     // a few keys: insert each one by rank (ballot) and a shift
                     for (int ii = 0; ii < tot; ++ii) {
                         const uint32_t v = wk[wcnt + ii];
@@ -342,7 +357,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     }
                 }
                 wcnt += tot;
-                if (tot && t > 0) publish();
+                if (grows && t > 0) publish();
                 if (wcnt > SW_CAP - 64)
                     wcnt = warp_compact_ge(wk, wi, wcnt, *reinterpret_cast<volatile uint32_t*>(&us.thr_key));
             }
