@@ -227,10 +227,6 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     }
                 }
             }
-            // The tile's logits are in registers: hand the stage back to the
-            // producer now, so the refill overlaps the filtering below.
-            __syncwarp();
-            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.empty[s])) : "memory");
             // max.NaN tree; oct[o] = max of values 8o..8o+7 (kept to screen octets)
             float mx16[16], oct[4];
 #pragma unroll
@@ -323,20 +319,16 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 // the warp's own m-th key: a new key below it cannot change the top-m list
                 const uint32_t own_mth = __shfl_sync(0xffffffffu, lkey, m - 1);
                 bool grows = false;
-#pragma unroll
-                for (int o = 0; o < 4; ++o) {
-                    if ((mm >> (8 * o)) & 0xFFu) {  // register indices stay static
-#pragma unroll
-                        for (int b = 8 * o; b < 8 * o + 8; ++b) {
-                            if (mm & (1u << b)) {
-                                const uint32_t key = fkey(vv[b]);
-                                grows |= key > own_mth;
-                                wk[pos] = key;
-                                wi[pos] = (int32_t)(a + 4 * (warp * 256 + lane + 32 * (b >> 2)) + (b & 3));
-                                ++pos;
-                            }
-                        }
-                    }
+                while (mm) {
+                    const int b = __ffs(mm) - 1;
+                    mm &= mm - 1;
+                    const int e = 4 * (warp * 256 + lane + 32 * (b >> 2)) + (b & 3);
+                    const float v = (e < bulk_n) ? st[e] : xr[a + e];
+                    const uint32_t key = fkey(v);
+                    grows |= key > own_mth;
+                    wk[pos] = key;
+                    wi[pos] = (int32_t)(a + e);
+                    ++pos;
                 }
                 __syncwarp();
                 grows = __any_sync(0xffffffffu, grows);
@@ -369,6 +361,9 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 if (wcnt > SW_CAP - 64)
                     wcnt = warp_compact_ge(wk, wi, wcnt, *reinterpret_cast<volatile uint32_t*>(&us.thr_key));
             }
+            // every lane of the warp is done with the stage: hand it back
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.empty[s])) : "memory");
             if (++s == S_STAGES) {
                 s = 0;
                 parity ^= 1u;
