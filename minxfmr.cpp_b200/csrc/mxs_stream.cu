@@ -21,7 +21,7 @@
 namespace mxs {
 
 constexpr int KSPLIT_K = 64;        // largest k of this path (register sort of 64)
-constexpr int SW_CAP = 256;         // candidates per consumer warp
+constexpr int SW_CAP = 128;         // candidates per consumer warp
 constexpr int SLOTS = 8;            // per-unit state ring (> the STAGES a warp can run ahead)
 constexpr int FCAP = 256;           // candidate buffer of a finish warp (longer lists stream through it)
 static_assert(KSPLIT_K == KSPLIT, "KSPLIT must match the register sort");
@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 }
                 wcnt += tot;
                 if (grows && t > 0) publish();
-                if (wcnt > SW_CAP - 64)
+                if (wcnt > SW_CAP - 40)
                     wcnt = warp_compact_ge(wk, wi, wcnt, *reinterpret_cast<volatile uint32_t*>(&us.thr_key));
             }
             // every lane of the warp is done with the stage: hand it back
