@@ -298,21 +298,70 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     tot = __shfl_sync(0xffffffffu, incl, 31);
                 }
                 if (wcnt + tot > SW_CAP) {
-                    // Make room: drop what the shared bound excludes; if that is
-                    // not enough, select (stream_shrink); filter the tile again.
-                    wcnt = warp_compact_ge(wk, wi, wcnt, *reinterpret_cast<volatile uint32_t*>(&us.thr_key));
-                    if (wcnt + tot > SW_CAP) stream_shrink(wk, wi, wcnt, k, whist, us);
-                    mm = pass_bits(bound());
-                    cc = __popc(mm);
-                    incl = warp_incl_scan(cc);
-                    tot = __shfl_sync(0xffffffffu, incl, 31);
-                    if (wcnt + tot > SW_CAP) {  // massive ties: the exact replay takes the row
-                        stopped = true;
-                        fl |= FLAG_OVERFLOW;
-                        mm = 0;
-                        cc = 0;
-                        incl = 0;
-                        tot = 0;
+                    // Does not fit (a loose bound, e.g. on the first tile): append
+                    // in rounds of at most two logits per lane (64 per warp), and
+                    // before each round make room: drop what the shared bound
+                    // excludes, then select (stream_shrink). Only if that cannot
+                    // free room (massive ties) does the replay take the row.
+                    uint32_t rest = mm;
+                    while (__any_sync(0xffffffffu, rest != 0u)) {
+                        if (wcnt > SW_CAP - 64) {
+                            wcnt = warp_compact_ge(wk, wi, wcnt, *reinterpret_cast<volatile uint32_t*>(&us.thr_key));
+                            if (wcnt > SW_CAP - 64) stream_shrink(wk, wi, wcnt, k, whist, us);
+                            if (wcnt > SW_CAP - 64) {
+                                stopped = true;
+                                fl |= FLAG_OVERFLOW;
+                                break;
+                            }
+                            // logits the raised bound excludes need not be appended
+                            const uint32_t tk = *reinterpret_cast<volatile uint32_t*>(&us.thr_key);
+                            uint32_t keep = 0u;
+                            for (uint32_t r2 = rest; r2; r2 &= r2 - 1) {
+                                const int b = __ffs(r2) - 1;
+                                const int e = 4 * (warp * 256 + lane + 32 * (b >> 2)) + (b & 3);
+                                if (fkey((e < bulk_n) ? st[e] : xr[a + e]) >= tk) keep |= 1u << b;
+                            }
+                            rest = keep;
+                        }
+                        uint32_t part = 0u;  // up to two of this lane's logits
+                        if (rest) {
+                            part = rest & (0u - rest);
+                            const uint32_t r1 = rest & ~part;
+                            if (r1) part |= r1 & (0u - r1);
+                        }
+                        rest &= ~part;
+                        const int cq = __popc(part);
+                        const int iq = warp_incl_scan(cq);
+                        const int tq = __shfl_sync(0xffffffffu, iq, 31);
+                        int pq = wcnt + iq - cq;
+                        for (; part; part &= part - 1) {
+                            const int b = __ffs(part) - 1;
+                            const int e = 4 * (warp * 256 + lane + 32 * (b >> 2)) + (b & 3);
+                            wk[pq] = fkey((e < bulk_n) ? st[e] : xr[a + e]);
+                            wi[pq] = (int32_t)(a + e);
+                            ++pq;
+                        }
+                        __syncwarp();
+                        wcnt += tq;
+                    }
+                    // The new keys were appended above. Rebuild the top-m list from
+                    // the buffer alone (distinct logits; merging it with the old
+                    // list could count a logit twice and break the bound).
+                    mm = 0;
+                    cc = 0;
+                    incl = 0;
+                    tot = 0;
+                    if (!stopped) {
+                        uint32_t top = 0u;  // lanes 0..m-1: running top-m of the buffer
+                        for (int r0 = 0; r0 < wcnt; r0 += 32 - m) {
+                            const int ii = r0 + lane - m;
+                            uint32_t v = top;
+                            if (lane >= m) v = (ii < wcnt) ? wk[ii] : 0u;
+                            v = warp_sort32_desc(v);
+                            top = (lane < m) ? v : 0u;
+                        }
+                        lkey = top;
+                        publish();
                     }
                 }
                 int pos = wcnt + incl - cc;
