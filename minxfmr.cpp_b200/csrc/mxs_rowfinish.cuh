@@ -156,14 +156,14 @@ __device__ __forceinline__ void block_draw(const Params& p, int64_t row, const E
 // every element is then offered serially.
 template <bool SMALL>
 __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int nan_state, unsigned char* region,
-                                            Misc& sm) {
+                                            Misc& sm, Ent* sheap) {
     const int tid = threadIdx.x;
     const int k = p.k_use;
     const int64_t V = p.vocab;
     const float* x = p.logits + row * p.ld;
     // SMALL: the heap lives in shared memory (k <= HEAP_SMEM_MAX); each case is
     // its own instantiation so every heap access has a known address space.
-    Ent* h = SMALL ? reinterpret_cast<Ent*>(region) : p.heap_ws + (int64_t)blockIdx.x * k;
+    Ent* h = SMALL ? sheap : p.heap_ws + (int64_t)blockIdx.x * k;
     Ent* xl = reinterpret_cast<Ent*>(region + HEAP_SMEM_MAX * sizeof(Ent));
     double* pbuf = SMALL ? reinterpret_cast<double*>(region + HEAP_SMEM_MAX * sizeof(Ent))
                          : p.prob_ws + (int64_t)blockIdx.x * k;
@@ -260,12 +260,14 @@ __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int na
 
 // Exact replay of the reference's partial_sort heap process over row `row`,
 // then the draw (see exact_row_t).
+// The heap of a small k lives at the start of `region` (exact_rows_kernel
+// passes a static __shared__ array to exact_row_t directly instead).
 __device__ __forceinline__ void exact_row(const Params& p, int64_t row, int nan_state, unsigned char* region,
                                           Misc& sm) {
     if (p.k_use <= HEAP_SMEM_MAX)
-        exact_row_t<true>(p, row, nan_state, region, sm);
+        exact_row_t<true>(p, row, nan_state, region, sm, reinterpret_cast<Ent*>(region));
     else
-        exact_row_t<false>(p, row, nan_state, region, sm);
+        exact_row_t<false>(p, row, nan_state, region, sm, nullptr);
 }
 
 }  // namespace mxs

@@ -614,6 +614,7 @@ __global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
 // One CTA per handed-over row (grid-stride over the list).
 __global__ void __launch_bounds__(NT, 1) exact_rows_kernel(Params p) {
     extern __shared__ __align__(128) unsigned char esmem[];
+    __shared__ Ent s_heap[HEAP_SMEM_MAX];
     Misc& sm = *reinterpret_cast<Misc*>(esmem + REGION_BYTES);
     const uint32_t n = *reinterpret_cast<volatile uint32_t*>(p.xcount);
     MXS_PROF_BEGIN();
@@ -621,7 +622,11 @@ __global__ void __launch_bounds__(NT, 1) exact_rows_kernel(Params p) {
     for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
         const int64_t row = p.xrows[i];
         const uint32_t f = p.row_flag[row];
-        exact_row(p, row, (f & FLAG_NAN) ? 1 : 0, esmem, sm);
+        if (p.k_use <= HEAP_SMEM_MAX) {
+            exact_row_t<true>(p, row, (f & FLAG_NAN) ? 1 : 0, esmem, sm, s_heap);
+        } else {
+            exact_row_t<false>(p, row, (f & FLAG_NAN) ? 1 : 0, esmem, sm, nullptr);
+        }
     }
     MXS_PROF_ADD(7, tt);
     MXS_PROF_FLUSH();
