@@ -440,6 +440,43 @@ __device__ inline int block_compact_ge(uint32_t* ckey, int32_t* cidx, Misc& sm, 
     return sm.cnt;
 }
 
+// Sort 32*NS packed entries held NS per lane (slot s of lane l = element
+// l + 32 s) descending, with a register bitonic network (warp-synchronous).
+template <int NS>
+__device__ __forceinline__ void warp_sort_desc(uint64_t (&a)[NS]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 32 * NS; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride >= 32) {
+                const int ss = stride / 32;
+#pragma unroll
+                for (int s = 0; s < NS; ++s) {
+                    if ((s & ss) == 0) {
+                        const int i = lane + 32 * s;
+                        const bool desc = ((i & size) == 0);
+                        const uint64_t x = a[s], y = a[s + ss];
+                        if ((x < y) == desc) {
+                            a[s] = y;
+                            a[s + ss] = x;
+                        }
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int s = 0; s < NS; ++s) {
+                    const int i = lane + 32 * s;
+                    const uint64_t o = __shfl_xor_sync(0xffffffffu, a[s], stride);
+                    const bool desc = ((i & size) == 0);
+                    const bool keep_max = (desc == ((i & stride) == 0));
+                    a[s] = keep_max ? (a[s] > o ? a[s] : o) : (a[s] < o ? a[s] : o);
+                }
+            }
+        }
+    }
+}
+
 // Sort a[0, P) descending, P a power of two <= SORTMAX (bitonic network).
 __device__ inline void block_sort_desc(uint64_t* a, int P) {
     if (P <= 64) {

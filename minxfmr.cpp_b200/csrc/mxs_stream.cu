@@ -20,7 +20,7 @@
 
 namespace mxs {
 
-constexpr int KSPLIT_K = 64;        // largest k of this path (register sort of 64)
+constexpr int KSPLIT_K = 128;       // largest k of this path (register sort of 128)
 constexpr int SW_CAP = 128;         // candidates per consumer warp
 constexpr int SLOTS = 8;            // per-unit state ring (> the STAGES a warp can run ahead)
 constexpr int FCAP = 256;           // candidate buffer of a finish warp (longer lists stream through it)
@@ -240,16 +240,21 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             if (t == 0) {
                 // Seeds from the unit's first tile, from each lane's largest and
                 // second largest logit (all distinct logits of the slice).
-                float m1 = -INFINITY, m2 = -INFINITY;
+                // top-2 per lane; for k > 64 also the 3rd and 4th (NaN-free
+                // screening below: a NaN row is replayed anyway)
+                float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY, m4 = -INFINITY;
 #pragma unroll
                 for (int b = 0; b < 32; ++b) {
                     if ((valid >> b) & 1u) {
                         const float x = vv[b];
                         if (x > m1) {
-                            m2 = m1;
-                            m1 = x;
+                            m4 = m3; m3 = m2; m2 = m1; m1 = x;
                         } else if (x > m2) {
-                            m2 = x;
+                            m4 = m3; m3 = m2; m2 = x;
+                        } else if (k > 64 && x > m3) {
+                            m4 = m3; m3 = x;
+                        } else if (k > 64 && x > m4) {
+                            m4 = x;
                         }
                     }
                 }
@@ -262,9 +267,12 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 uint32_t own;
                 if (k <= 32) {
                     own = __shfl_sync(0xffffffffu, sorted1, k - 1);
-                } else {
+                } else if (k <= 64) {
                     const uint32_t sorted2 = warp_sort32_desc(nv >= 2 ? fkey(m2) : 0u);
                     own = __shfl_sync(0xffffffffu, sorted2, (k + 1) / 2 - 1);
+                } else {  // the ceil(k/4)-th largest lane 4th-maximum: 4 logits per such lane
+                    const uint32_t sorted4 = warp_sort32_desc(nv >= 4 ? fkey(m4) : 0u);
+                    own = __shfl_sync(0xffffffffu, sorted4, (k + 3) / 4 - 1);
                 }
                 wseed = bound_of(own);
                 lkey = (lane < m) ? sorted1 : 0u;
@@ -511,6 +519,53 @@ __device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, doub
     return __shfl_sync(0xffffffffu, pick, 0);
 }
 
+// Sort the cnt (<= 32*NS) survivors, find ties, draw. Returns true when the
+// row still needs the replay (a tie and a requested top-k list, or a draw that
+// lands on a tied position).
+template <int NS>
+__device__ __forceinline__ bool finish_sorted(const Params& p, int64_t row, FinishWarpSmem& w, int cnt, int k,
+                                              bool tie, int lane) {
+    uint64_t b[NS];
+#pragma unroll
+    for (int s2 = 0; s2 < NS; ++s2) {
+        const int i = lane + 32 * s2;
+        b[s2] = i < cnt ? ((uint64_t)w.keys[i] << 32) | (uint32_t)w.idx[i] : 0ull;
+    }
+    warp_sort_desc<NS>(b);
+    // tied[i]: position i < k holds a value equal to a neighbour among the cnt sorted
+    uint32_t tm[NS];
+#pragma unroll
+    for (int s2 = 0; s2 < NS; ++s2) {
+        const uint64_t up = __shfl_up_sync(0xffffffffu, b[s2], 1);
+        const uint64_t dn = __shfl_down_sync(0xffffffffu, b[s2], 1);
+        const uint64_t prev_last = __shfl_sync(0xffffffffu, b[s2 > 0 ? s2 - 1 : 0], 31);
+        const uint64_t next_first = __shfl_sync(0xffffffffu, b[s2 + 1 < NS ? s2 + 1 : s2], 0);
+        const int i = lane + 32 * s2;
+        const uint64_t pv = (lane == 0) ? prev_last : up;   // position i - 1 (valid when i > 0)
+        const uint64_t nx = (lane == 31) ? next_first : dn;  // position i + 1 (valid when i + 1 < 32 NS)
+        const bool t = i < k && ((i > 0 && (b[s2] >> 32) == (pv >> 32)) ||
+                                 (i + 1 < cnt && (b[s2] >> 32) == (nx >> 32)));
+        tm[s2] = __ballot_sync(0xffffffffu, t);
+    }
+    uint32_t any = 0u;
+#pragma unroll
+    for (int s2 = 0; s2 < NS; ++s2) any |= tm[s2];
+    tie = tie || any != 0u;
+    if (tie && p.topk_idx) return true;
+#pragma unroll
+    for (int s2 = 0; s2 < NS; ++s2) {
+        const int i = lane + 32 * s2;
+        if (i < k) w.e[i] = Ent{fkey_inv((uint32_t)(b[s2] >> 32)), (int32_t)(uint32_t)b[s2]};
+    }
+    __syncwarp();
+    const int pick = warp_draw(p, row, w.e, k, w.pbuf);
+    uint32_t tp = 0u;
+#pragma unroll
+    for (int s2 = 0; s2 < NS; ++s2)
+        if ((pick >> 5) == s2) tp = tm[s2];
+    return tie && ((tp >> (pick & 31)) & 1u);
+}
+
 __global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
     extern __shared__ __align__(16) unsigned char fsmem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -572,32 +627,10 @@ __global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
             exact = true;
         }
         if (!exact) {
-            uint64_t b0 = lane < cnt ? ((uint64_t)w.keys[lane] << 32) | (uint32_t)w.idx[lane] : 0ull;
-            uint64_t b1 = lane + 32 < cnt ? ((uint64_t)w.keys[lane + 32] << 32) | (uint32_t)w.idx[lane + 32] : 0ull;
-            warp_sort64_desc(b0, b1);
-            const uint64_t first1 = __shfl_sync(0xffffffffu, b1, 0);
-            const uint64_t last0 = __shfl_sync(0xffffffffu, b0, 31);
-            const uint64_t dn0 = __shfl_down_sync(0xffffffffu, b0, 1);
-            const uint64_t dn1 = __shfl_down_sync(0xffffffffu, b1, 1);
-            const uint64_t up0 = __shfl_up_sync(0xffffffffu, b0, 1);
-            const uint64_t up1 = __shfl_up_sync(0xffffffffu, b1, 1);
-            const uint64_t n0 = (lane == 31) ? first1 : dn0;   // position lane + 1
-            const uint64_t pr1 = (lane == 0) ? last0 : up1;     // position lane + 31
-            // tied[i]: position i < k holds a value equal to a neighbour among the cnt sorted
-            const bool t0 = lane < k && ((lane > 0 && (b0 >> 32) == (up0 >> 32)) ||
-                                         (lane + 1 < cnt && (b0 >> 32) == (n0 >> 32)));
-            const bool t1 = lane + 32 < k && (((b1 >> 32) == (pr1 >> 32)) ||
-                                              (lane + 33 < cnt && (b1 >> 32) == (dn1 >> 32)));
-            const uint32_t tm0 = __ballot_sync(0xffffffffu, t0), tm1 = __ballot_sync(0xffffffffu, t1);
-            tie = tie || (tm0 | tm1) != 0u;
-            if (tie && p.topk_idx) exact = true;
-            if (!exact) {
-                if (lane < k) w.e[lane] = Ent{fkey_inv((uint32_t)(b0 >> 32)), (int32_t)(uint32_t)b0};
-                if (lane + 32 < k) w.e[lane + 32] = Ent{fkey_inv((uint32_t)(b1 >> 32)), (int32_t)(uint32_t)b1};
-                __syncwarp();
-                const int pick = warp_draw(p, row, w.e, k, w.pbuf);
-                if (tie && (((pick < 32 ? tm0 : tm1) >> (pick & 31)) & 1u)) exact = true;
-            }
+            if (cnt <= 64)
+                exact = finish_sorted<2>(p, row, w, cnt, k, tie, lane);
+            else
+                exact = finish_sorted<4>(p, row, w, cnt, k, tie, lane);
         }
     }
     if (lane == 0) {

@@ -5,7 +5,7 @@
 
 namespace mxs {
 struct Params;
-constexpr int KSPLIT = 64;           // largest k the three-kernel path takes
+constexpr int KSPLIT = 128;          // largest k the three-kernel path takes
 constexpr int SPLIT_ROW_CAP = 1024;  // candidate list entries per row
 constexpr int S_TILE = 8192;         // logits per ring stage of the streaming kernel (32 KB)
 constexpr int S_STAGES = 3;          // ring depth (96 KB in flight per CTA)
