@@ -240,21 +240,35 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             if (t == 0) {
                 // Seeds from the unit's first tile, from each lane's largest and
                 // second largest logit (all distinct logits of the slice).
-                // top-2 per lane; for k > 64 also the 3rd and 4th (NaN-free
-                // screening below: a NaN row is replayed anyway)
-                float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY, m4 = -INFINITY;
+                // top-2 per lane (for k > 64 also the 3rd and 4th, in a loop of its own)
+                float m1 = -INFINITY, m2 = -INFINITY, m4 = -INFINITY;
+                if (k <= 64) {
 #pragma unroll
-                for (int b = 0; b < 32; ++b) {
-                    if ((valid >> b) & 1u) {
-                        const float x = vv[b];
-                        if (x > m1) {
-                            m4 = m3; m3 = m2; m2 = m1; m1 = x;
-                        } else if (x > m2) {
-                            m4 = m3; m3 = m2; m2 = x;
-                        } else if (k > 64 && x > m3) {
-                            m4 = m3; m3 = x;
-                        } else if (k > 64 && x > m4) {
-                            m4 = x;
+                    for (int b = 0; b < 32; ++b) {
+                        if ((valid >> b) & 1u) {
+                            const float x = vv[b];
+                            if (x > m1) {
+                                m2 = m1;
+                                m1 = x;
+                            } else if (x > m2) {
+                                m2 = x;
+                            }
+                        }
+                    }
+                } else {
+                    float m3 = -INFINITY;
+                    for (int b = 0; b < 32; ++b) {
+                        if ((valid >> b) & 1u) {
+                            const float x = vv[b];
+                            if (x > m1) {
+                                m4 = m3; m3 = m2; m2 = m1; m1 = x;
+                            } else if (x > m2) {
+                                m4 = m3; m3 = m2; m2 = x;
+                            } else if (x > m3) {
+                                m4 = m3; m3 = x;
+                            } else if (x > m4) {
+                                m4 = x;
+                            }
                         }
                     }
                 }
