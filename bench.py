@@ -280,7 +280,7 @@ def main():
                                        "one uniform per row", "rows_per_gpu": rows, "vocab": V, "top_k": TOP_K,
                            "temperature": TEMPERATURE, "parallelism": f"row-sharded x{world}, no collective",
                            "l2": "inputs (2.49 GB per GPU) larger than L2; no flush"},
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 3 * args.steps,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps,
                 "hbm_frac_of_8tbs": achieved / 8000.0, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -35,6 +35,10 @@ struct Device {
     int blocks_per_sm = 0;
     void* ws = nullptr;  // library-owned workspace (zeroed at allocation)
     cudaEvent_t ev_start = nullptr, ev_stop = nullptr;  // mxs_set_profile_events
+    // The two-kernel path leaves its per-row counters clear; a call with the
+    // same layout on the library workspace can skip clearing them again.
+    int64_t clean_rows = -1;
+    size_t clean_off = 0;
     size_t ws_bytes = 0;
     HostBuffers hb;
 };
@@ -70,7 +74,7 @@ struct Plan {
     int k_use = 1;
     int S = 1, tpc = 1, grid = 1, outcap = 0;
     bool split = false;  // three-kernel path (stream -> finish -> exact)
-    size_t off_rcand = 0, off_rcnt = 0, off_rflag = 0, off_xcount = 0, off_xrows = 0, zero_bytes = 0;
+    size_t off_rcand = 0, off_rcnt = 0, off_rflag = 0, zero_bytes = 0;
     int64_t units = 0;
     size_t off_counter = 0, off_state = 0, off_status = 0, off_ccount = 0, off_cand = 0, off_heap = 0,
            off_prob = 0, total = 0;
@@ -141,14 +145,12 @@ Plan make_plan(const Device& d, int64_t rows, int64_t vocab, int k_use, bool mer
     o = align_up(o + sizeof(uint32_t) * (size_t)full, 256);
     pl.off_ccount = o;
     if (split) {
-        // per-row counters, flags and the exact-row count: cleared by every call
+        // per-row counters and flags: must read zero when a call starts; the
+        // finish kernel clears them after use
         pl.off_rcnt = o;
         pl.off_rflag = pl.off_rcnt + sizeof(uint32_t) * (size_t)rows;
-        pl.off_xcount = pl.off_rflag + sizeof(uint32_t) * (size_t)rows;
-        pl.zero_bytes = pl.off_xcount + 16 - pl.off_rcnt;
-        o = align_up(pl.off_xcount + 16, 256);
-        pl.off_xrows = o;
-        o = align_up(o + sizeof(int32_t) * (size_t)rows, 256);
+        pl.zero_bytes = 2 * sizeof(uint32_t) * (size_t)rows;
+        o = align_up(pl.off_rflag + sizeof(uint32_t) * (size_t)rows, 256);
         pl.off_rcand = o;
         o = align_up(o + sizeof(uint64_t) * (size_t)rows * split_row_cap(pl.S), 256);
     } else if (pl.S > 1) {
@@ -175,6 +177,7 @@ int ensure_library_ws(Device& d, size_t bytes, cudaStream_t stream) {
         d.ws = nullptr;
         d.ws_bytes = 0;
     }
+    d.clean_rows = -1;
     size_t want = std::max<size_t>(bytes, 1 << 20);
     if (cudaMalloc(&d.ws, want) != cudaSuccess) return MXS_ERR_CUDA;
     if (cudaMemsetAsync(d.ws, 0, want, stream) != cudaSuccess) return MXS_ERR_CUDA;
@@ -196,8 +199,6 @@ void fill_workspace(Params& p, const Plan& pl, void* ws) {
         p.row_cnt = reinterpret_cast<uint32_t*>(b + pl.off_rcnt);
         p.row_flag = reinterpret_cast<uint32_t*>(b + pl.off_rflag);
         p.row_cap = split_row_cap(pl.S);
-        p.xcount = reinterpret_cast<uint32_t*>(b + pl.off_xcount);
-        p.xrows = reinterpret_cast<int32_t*>(b + pl.off_xrows);
     }
 }
 
@@ -208,7 +209,7 @@ void clamp_p(double* top_p, double* min_p) {  // src/api/minxfmr.cpp:2109-2111
 }
 
 int launch(Params& p, const Plan& pl, cudaStream_t stream, int sms = 148, cudaEvent_t ev0 = nullptr,
-           cudaEvent_t ev1 = nullptr) {
+           cudaEvent_t ev1 = nullptr, Device* lib_ws_owner = nullptr) {
     p.S = pl.S;
     p.tiles_per_chunk = pl.tpc;
     p.units = pl.units;
@@ -218,10 +219,17 @@ int launch(Params& p, const Plan& pl, cudaStream_t stream, int sms = 148, cudaEv
         // n-th tile, so its consumers' bounded wait runs out (MXS_ROW_TIMEOUT).
         const char* dt = getenv("MXS_DEBUG_DROP_TILE");
         p.debug_drop_tile = dt ? atoll(dt) : -1;
-        if (cudaMemsetAsync(p.row_cnt, 0, pl.zero_bytes, stream) != cudaSuccess) return MXS_ERR_CUDA;
+        const bool clean = lib_ws_owner && lib_ws_owner->clean_rows == p.rows && lib_ws_owner->clean_off == pl.off_rcnt;
+        if (lib_ws_owner) lib_ws_owner->clean_rows = -1;
+        if (!clean && cudaMemsetAsync(p.row_cnt, 0, pl.zero_bytes, stream) != cudaSuccess) return MXS_ERR_CUDA;
         if (mxs::stream_path_launch(p, pl.grid, sms, stream, ev0, ev1) != cudaSuccess) return MXS_ERR_CUDA;
+        if (lib_ws_owner) {
+            lib_ws_owner->clean_rows = p.rows;
+            lib_ws_owner->clean_off = pl.off_rcnt;
+        }
         return MXS_OK;
     }
+    if (lib_ws_owner) lib_ws_owner->clean_rows = -1;
     const bool tma = (reinterpret_cast<uintptr_t>(p.logits) % 16 == 0) && (p.ld % 4 == 0);
     // MXS_SAMPLER_BLOCK_PATH=1 selects the CTA-synchronous streaming kernel for
     // every k (the parity tests run both kernels).
@@ -299,7 +307,7 @@ int mxs_sample_topk_ex(const float* d_logits, int64_t rows, int64_t vocab, int64
     p.row_flags = d_row_flags;
     p.mode = mxs::MODE_SAMPLE;
     fill_workspace(p, pl, ws);
-    return launch(p, pl, (cudaStream_t)stream, d->sms, d->ev_start, d->ev_stop);
+    return launch(p, pl, (cudaStream_t)stream, d->sms, d->ev_start, d->ev_stop, d_workspace ? nullptr : d);
 }
 
 int mxs_sample_topk(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
@@ -397,6 +405,7 @@ int mxs_shard_candidates(const float* d_shard_logits, int64_t rows, int64_t shar
     p.out_count = d_count;
     p.out_flags = d_flags;
     p.out_cap = cap;
+    d->clean_rows = -1;
     fill_workspace(p, pl, d->ws);
     return launch(p, pl, (cudaStream_t)stream);
 }
@@ -437,6 +446,7 @@ int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count_all, co
     p.in_flags = d_flags_all;
     p.nshards = nshards;
     p.in_cap = cap;
+    d->clean_rows = -1;
     fill_workspace(p, pl, d->ws);
     p.logits = nullptr;
     // no logits: launch the plain variant (no bulk copies are issued in merge mode)

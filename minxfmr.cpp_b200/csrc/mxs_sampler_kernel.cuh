@@ -72,15 +72,13 @@ struct Params {
     int nshards, in_cap;
     int force_block_path;      // 1: use the CTA-synchronous streaming kernel even where the
                                // warp-specialised one applies (tests cover both)
-    // three-kernel path (k <= KSPLIT): stream -> per-row candidate lists -> finish -> exact
+    // two-kernel path (k <= KSPLIT): stream -> per-row candidate lists -> finish (+ replay)
     uint64_t* row_cand;        // rows x row_cap, (key << 32) | column
     uint32_t* row_cnt;         // rows: entries appended (may exceed row_cap: overflow)
     uint32_t* row_flag;        // rows: OR of FLAG_* seen while streaming
     int row_cap;
-    uint32_t* xcount;          // rows handed to the exact kernel
     int64_t debug_drop_tile;   // test hook (MXS_DEBUG_DROP_TILE): the streaming producer stops before
                                // the CTA-0 tile with this sequence number; -1 = off
-    int32_t* xrows;            // rows: their indices
 };
 constexpr int MODE_SAMPLE = 0;
 constexpr int MODE_EMIT = 1;

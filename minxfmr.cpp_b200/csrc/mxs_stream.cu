@@ -1,4 +1,4 @@
-// Three-kernel sampling path for k <= KSPLIT on 16-byte aligned rows.
+// Two-kernel sampling path for k <= KSPLIT on 16-byte aligned rows.
 //
 //  1. stream_select_kernel: a producer warp streams every tile of the CTA's
 //     (row, chunk) units through a bulk-copy ring; 8 consumer warps each filter
@@ -9,8 +9,9 @@
 //     global memory when it leaves the unit.
 //  2. finish_rows_kernel: one warp per row selects the k-th largest candidate,
 //     sorts the k survivors in registers, checks for ties and draws.
-//  3. exact_rows_kernel: one CTA per row the finish kernel handed over (a tie,
-//     a NaN, an overflow) replays the reference's heap process over the row.
+//  3. then the finish kernel's CTA (8 warps = one replay CTA) replays each of
+//     its rows that needs it (a tie, a NaN, an overflow): the reference's heap
+//     process over the row.
 #include <cmath>
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -580,12 +581,11 @@ __device__ __forceinline__ bool finish_sorted(const Params& p, int64_t row, Fini
     return tie && ((tp >> (pick & 31)) & 1u);
 }
 
-__global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
-    extern __shared__ __align__(16) unsigned char fsmem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    FinishWarpSmem& w = reinterpret_cast<FinishWarpSmem*>(fsmem)[warp];
-    const int64_t row = (int64_t)blockIdx.x * F_WARPS + warp;
-    if (row >= p.rows) return;
+// One warp finishes row `row`; a row that needs the replay is listed in
+// s_xrow/s_xflag for the CTA. The row's counters are cleared for the next call.
+__device__ void finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w, int64_t* s_xrow, uint32_t* s_xflag,
+                                int* s_xn) {
+    const int lane = threadIdx.x & 31;
     const int k = p.k_use;
     uint32_t flags = p.row_flag[row];
     const uint32_t cnt_all = p.row_cnt[row];
@@ -652,56 +652,51 @@ __global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
             p.next[row] = -1;
             atomicOr(p.status, flags);
         } else if (exact) {
-            p.xrows[atomicAdd(p.xcount, 1u)] = (int32_t)row;
+            const int at = atomicAdd(s_xn, 1);
+            s_xrow[at] = row;
+            s_xflag[at] = flags;
         }
         if (p.row_flags) p.row_flags[row] = flags | ((exact && !(flags & FLAG_TIMEOUT)) ? FLAG_EXACT : 0u);
+        p.row_cnt[row] = 0u;  // left clear for the next call on this workspace
+        p.row_flag[row] = 0u;
     }
 }
 
-// One CTA per handed-over row (grid-stride over the list).
-__global__ void __launch_bounds__(NT, 1) exact_rows_kernel(Params p) {
-    extern __shared__ __align__(128) unsigned char esmem[];
+// Rows of the exact replay need a whole CTA; the finish kernel's CTAs are
+// exactly NT threads (F_WARPS warps) and replay their own handed-over rows.
+constexpr size_t F_WARP_AREA = sizeof(FinishWarpSmem) * F_WARPS;
+constexpr size_t F_REGION = F_WARP_AREA > REGION_BYTES ? F_WARP_AREA : REGION_BYTES;
+constexpr size_t F_SMEM = (F_REGION + 15) / 16 * 16 + sizeof(Misc);
+static_assert(F_WARPS * 32 == NT, "the replay needs a CTA of NT threads");
+
+__global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
+    extern __shared__ __align__(128) unsigned char fsmem[];
     __shared__ Ent s_heap[HEAP_SMEM_MAX];
-    Misc& sm = *reinterpret_cast<Misc*>(esmem + REGION_BYTES);
-    const uint32_t n = *reinterpret_cast<volatile uint32_t*>(p.xcount);
-    MXS_PROF_BEGIN();
-    MXS_PROF_T0(tt);
-    for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
-        const int64_t row = p.xrows[i];
-        const uint32_t f = p.row_flag[row];
-        if (p.k_use <= HEAP_SMEM_MAX) {
-            exact_row_t<true>(p, row, (f & FLAG_NAN) ? 1 : 0, esmem, sm, s_heap);
-        } else {
-            exact_row_t<false>(p, row, (f & FLAG_NAN) ? 1 : 0, esmem, sm, nullptr);
-        }
-    }
-    MXS_PROF_ADD(7, tt);
-    MXS_PROF_FLUSH();
+    __shared__ int64_t s_xrow[F_WARPS];
+    __shared__ uint32_t s_xflag[F_WARPS];
+    __shared__ int s_xn;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    FinishWarpSmem& w = reinterpret_cast<FinishWarpSmem*>(fsmem)[warp];
+    const int64_t row = (int64_t)blockIdx.x * F_WARPS + warp;
+    if (threadIdx.x == 0) s_xn = 0;
+    csync();
+    if (row < p.rows) finish_row_warp(p, row, w, s_xrow, s_xflag, &s_xn);
+    csync();
+    // the CTA replays the rows its warps handed over
+    Misc& sm = *reinterpret_cast<Misc*>(fsmem + (F_REGION + 15) / 16 * 16);
+    const int n = s_xn;
+    for (int i = 0; i < n; ++i)
+        exact_row_t<true>(p, s_xrow[i], (s_xflag[i] & FLAG_NAN) ? 1 : 0, fsmem, sm, s_heap);
 }
 
-#ifdef MXS_PROFILE
-// Phase timers of the exact kernel: 0 filter, 1 offers, 2 sort+draw, 3 build,
-// 4 offers made (count), 5 steps (count), 7 total.
-extern "C" __attribute__((visibility("default"))) int mxs_prof_read_exact(unsigned long long* host, int clear) {
-    if (cudaMemcpyFromSymbol(host, g_mxs_prof, sizeof(g_mxs_prof)) != cudaSuccess) return -3;
-    if (clear) {
-        static unsigned long long zeros[PROF_CTAS][PROF_PHASES];
-        if (cudaMemcpyToSymbol(g_mxs_prof, zeros, sizeof(zeros)) != cudaSuccess) return -3;
-    }
-    return 0;
-}
-#endif
+
 
 size_t stream_smem_bytes() { return S_SMEM; }
 
 cudaError_t stream_path_configure(int* blocks_per_sm) {
     cudaError_t e = cudaFuncSetAttribute(stream_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(finish_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(sizeof(FinishWarpSmem) * F_WARPS));
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(exact_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(REGION_BYTES + sizeof(Misc)));
+    e = cudaFuncSetAttribute(finish_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F_SMEM);
     if (e != cudaSuccess) return e;
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, stream_select_kernel, NT_WS, S_SMEM);
 }
@@ -713,11 +708,7 @@ cudaError_t stream_path_launch(const Params& p, int grid, int exact_grid, cudaSt
     cudaError_t e = cudaGetLastError();
     if (ev_stop) cudaEventRecord(ev_stop, stream);
     if (e != cudaSuccess) return e;
-    finish_rows_kernel<<<(unsigned)((p.rows + F_WARPS - 1) / F_WARPS), F_WARPS * 32, sizeof(FinishWarpSmem) * F_WARPS,
-                         stream>>>(p);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    exact_rows_kernel<<<exact_grid, NT, REGION_BYTES + sizeof(Misc), stream>>>(p);
+    finish_rows_kernel<<<(unsigned)((p.rows + F_WARPS - 1) / F_WARPS), F_WARPS * 32, F_SMEM, stream>>>(p);
     return cudaGetLastError();
 }
 
