@@ -219,6 +219,11 @@ int launch(Params& p, const Plan& pl, cudaStream_t stream, int sms = 148, cudaEv
         // n-th tile, so its consumers' bounded wait runs out (MXS_ROW_TIMEOUT).
         const char* dt = getenv("MXS_DEBUG_DROP_TILE");
         p.debug_drop_tile = dt ? atoll(dt) : -1;
+        // MXS_REPLAY_WARP_MIN=n (tests): replay a finish CTA's tie rows one per
+        // warp when it holds n or more of them (default 2; 1 = always per warp,
+        // 9 = always with the whole CTA).
+        const char* rw = getenv("MXS_REPLAY_WARP_MIN");
+        p.replay_warp_min = rw ? atoi(rw) : 2;
         const bool clean = lib_ws_owner && lib_ws_owner->clean_rows == p.rows && lib_ws_owner->clean_off == pl.off_rcnt;
         if (lib_ws_owner) lib_ws_owner->clean_rows = -1;
         if (!clean && cudaMemsetAsync(p.row_cnt, 0, pl.zero_bytes, stream) != cudaSuccess) return MXS_ERR_CUDA;

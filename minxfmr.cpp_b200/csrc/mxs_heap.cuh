@@ -92,4 +92,99 @@ __device__ __forceinline__ void heap_sort(Ent* h, int len) {
     }
 }
 
+// Top-down replacement of the root, for heaps holding no NaN: the hole takes
+// the same child path as heap_place but stops at the first child holding a
+// value strictly greater than e. With every value ordered, the heap property
+// makes the values along that path non-decreasing, so heap_place's sift-up
+// would stop at the same spot; the resulting heap is identical. The oracle's
+// mode 2 restates this and is checked against std::partial_sort. Both
+// versions return the new root value.
+//
+// One level per step: for warps that replay rows side by side (many warps
+// hide each other's latency; fewer instructions and registers win there).
+__device__ __forceinline__ float heap_place_top1(Ent* h, int len, Ent e) {
+    int hole = 0;
+    float root = e.v;
+    for (;;) {
+        int c = 2 * hole + 1;
+        if (c >= len) break;
+        Ent ch = h[c];
+        if (c + 1 < len) {
+            const Ent r = h[c + 1];
+            if (!before(r.v, ch.v)) {
+                ch = r;
+                ++c;
+            }
+        }
+        if (before(ch.v, e.v)) break;
+        h[hole] = ch;
+        if (hole == 0) root = ch.v;
+        hole = c;
+    }
+    h[hole] = e;
+    return root;
+}
+
+// Two levels per step: for a lone thread replaying a row (latency-bound).
+__device__ __forceinline__ float heap_place_top2(Ent* h, int len, Ent e) {
+    // Two levels per round: the children and the four grandchildren of the
+    // hole are loaded together, so one shared-memory round trip serves both
+    // decisions. Loads at or past len are skipped.
+    int hole = 0;
+    float root = e.v;
+    for (;;) {
+        const int c = 2 * hole + 1;
+        if (c >= len) break;
+        const int gc = 2 * c + 1;  // first grandchild
+        Ent l = h[c], r = l, g0 = l, g1 = l, g2 = l, g3 = l;
+        if (c + 1 < len) r = h[c + 1];
+        if (gc < len) g0 = h[gc];
+        if (gc + 1 < len) g1 = h[gc + 1];
+        if (gc + 2 < len) g2 = h[gc + 2];
+        if (gc + 3 < len) g3 = h[gc + 3];
+        const bool take_r = (c + 1 < len) && !before(r.v, l.v);
+        const Ent ch = take_r ? r : l;
+        if (before(ch.v, e.v)) break;
+        h[hole] = ch;
+        if (hole == 0) root = ch.v;
+        hole = c + (take_r ? 1 : 0);
+        const int c2 = 2 * hole + 1;
+        if (c2 >= len) break;
+        const Ent l2 = take_r ? g2 : g0, r2 = take_r ? g3 : g1;
+        const bool take_r2 = (c2 + 1 < len) && !before(r2.v, l2.v);
+        const Ent ch2 = take_r2 ? r2 : l2;
+        if (before(ch2.v, e.v)) break;
+        h[hole] = ch2;
+        hole = c2 + (take_r2 ? 1 : 0);
+    }
+    h[hole] = e;
+    return root;
+}
+
+template <bool LOOKAHEAD>
+__device__ __forceinline__ float heap_place_top(Ent* h, int len, Ent e) {
+    return LOOKAHEAD ? heap_place_top2(h, len, e) : heap_place_top1(h, len, e);
+}
+
+// Offers list[0, n) in order to a heap without NaN; returns the root value.
+template <bool LOOKAHEAD>
+__device__ __forceinline__ float heap_offer_list_top(Ent* h, int len, const Ent* list, int n, float root) {
+    for (int i = 0; i < n; ++i) {
+        const Ent e = list[i];
+        if (before(e.v, root)) root = heap_place_top<LOOKAHEAD>(h, len, e);
+    }
+    return root;
+}
+
+// heap_sort for heaps without NaN (same result, top-down replacements).
+template <bool LOOKAHEAD>
+__device__ __forceinline__ void heap_sort_top(Ent* h, int len) {
+    while (len > 1) {
+        --len;
+        const Ent e = h[len];
+        h[len] = h[0];
+        heap_place_top<LOOKAHEAD>(h, len, e);
+    }
+}
+
 }  // namespace mxs

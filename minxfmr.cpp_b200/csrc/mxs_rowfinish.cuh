@@ -231,12 +231,10 @@ __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int na
                 }
                 MXS_PROF_ADD(0, tfl);
                 MXS_PROF_T0(tof);
-                if (tid == 0) {
-                    for (int w2 = 0; w2 < NWARPS; ++w2) {
-                        const Ent* sl = xl + w2 * SLOT;
-                        const int n2 = sm.warp_tot[w2];
-                        for (int i = 0; i < n2; ++i) heap_offer(h, k, sl[i]);
-                    }
+                if (tid == 0) {  // no NaN here: top-down replacements
+                    float root = h[0].v;
+                    for (int w2 = 0; w2 < NWARPS; ++w2)
+                        root = heap_offer_list_top<true>(h, k, xl + w2 * SLOT, sm.warp_tot[w2], root);
                 }
                 csync();
                 MXS_PROF_ADD(1, tof);
@@ -252,7 +250,12 @@ __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int na
         }
     }
     MXS_PROF_T0(tsd);
-    if (tid == 0) heap_sort(h, k);
+    if (tid == 0) {
+        if (nan_state)
+            heap_sort(h, k);
+        else
+            heap_sort_top<true>(h, k);
+    }
     csync();
     block_draw(p, row, h, k, pbuf, sm);
     MXS_PROF_ADD(2, tsd);

@@ -77,6 +77,8 @@ struct Params {
     uint32_t* row_cnt;         // rows: entries appended (may exceed row_cap: overflow)
     uint32_t* row_flag;        // rows: OR of FLAG_* seen while streaming
     int row_cap;
+    int replay_warp_min;       // the finish kernel replays tie rows one per warp when its CTA holds at
+                               // least this many of them, else with the whole CTA (MXS_REPLAY_WARP_MIN)
     int64_t debug_drop_tile;   // test hook (MXS_DEBUG_DROP_TILE): the streaming producer stops before
                                // the CTA-0 tile with this sequence number; -1 = off
 };

@@ -581,10 +581,96 @@ __device__ __forceinline__ bool finish_sorted(const Params& p, int64_t row, Fini
     return tie && ((tp >> (pick & 31)) & 1u);
 }
 
-// One warp finishes row `row`; a row that needs the replay is listed in
-// s_xrow/s_xflag for the CTA. The row's counters are cleared for the next call.
-__device__ void finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w, int64_t* s_xrow, uint32_t* s_xflag,
-                                int* s_xn) {
+// One warp replays the reference's partial_sort heap process over row `row`
+// (the process exact_row_t emulates with a whole CTA) and draws. For rows
+// without NaN, k <= KSPLIT_K. The heap lives in w.e; w.keys/w.idx hold the
+// replay list. The row is read once, in batches of 512 logits (4 float4 per
+// lane, the next batch in flight while one is filtered); every logit above the
+// root seen at the last offer goes to the list in index order, and lane 0
+// offers the list whenever it could not take another quarter batch. The root
+// only rises (no NaN), so a stale root lets through a superset of the logits
+// that enter, and each offer makes the exact comparison itself.
+constexpr int XSLOT = FCAP;  // Ent entries in w.keys + w.idx
+static_assert(sizeof(uint32_t) * FCAP * 2 == sizeof(Ent) * XSLOT, "replay list overlays keys and idx");
+
+__device__ __forceinline__ void xload4(const float* x, int64_t j, int64_t V, float4& v) {
+    if (j + 3 < V) {
+        v = __ldg(reinterpret_cast<const float4*>(x + j));
+    } else {
+        v.x = j < V ? x[j] : 0.f;
+        v.y = j + 1 < V ? x[j + 1] : 0.f;
+        v.z = j + 2 < V ? x[j + 2] : 0.f;
+        v.w = 0.f;
+    }
+}
+
+__device__ void exact_row_warp(const Params& p, int64_t row, FinishWarpSmem& w) {
+    const int lane = threadIdx.x & 31;
+    const int k = p.k_use;
+    const int64_t V = p.vocab;
+    const float* x = p.logits + row * p.ld;
+    Ent* h = w.e;
+    Ent* slot = reinterpret_cast<Ent*>(w.keys);
+    for (int i = lane; i < k; i += 32) h[i] = Ent{x[i], i};
+    __syncwarp();
+    if (lane == 0) heap_build(h, k);
+    __syncwarp();
+    if (k < V) {
+        float r0 = h[0].v;
+        int c = 0;
+        const int64_t g0 = (int64_t)k & ~(int64_t)3;  // rows start 16-byte aligned on this path
+        float4 nx[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int64_t j = g0 + 128 * q + 4 * lane;
+            if (j < V) xload4(x, j, V, nx[q]);
+        }
+        for (int64_t g = g0; g < V; g += 512) {
+            float4 cur[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) cur[q] = nx[q];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int64_t j = g + 512 + 128 * q + 4 * lane;
+                if (j < V) xload4(x, j, V, nx[q]);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (c > XSLOT - 128) {
+                    __syncwarp();
+                    if (lane == 0) heap_offer_list_top<false>(h, k, slot, c, r0);
+                    __syncwarp();
+                    r0 = h[0].v;
+                    c = 0;
+                }
+                const int64_t j = g + 128 * q + 4 * lane;
+                const float e4[4] = {cur[q].x, cur[q].y, cur[q].z, cur[q].w};
+                uint32_t m = 0u;
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    if (j + t >= k && j + t < V && e4[t] > r0) m |= 1u << t;
+                const int n = __popc(m);
+                const int incl = warp_incl_scan(n);
+                int at = c + incl - n;
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    if (m & (1u << t)) slot[at++] = Ent{e4[t], (int32_t)(j + t)};
+                c += __shfl_sync(0xffffffffu, incl, 31);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) heap_offer_list_top<false>(h, k, slot, c, r0);
+        __syncwarp();
+    }
+    if (lane == 0) heap_sort_top<false>(h, k);
+    __syncwarp();
+    warp_draw(p, row, h, k, w.pbuf);
+    __syncwarp();
+}
+
+// One warp finishes row `row`; returns true (in every lane) when the row needs
+// the replay. The row's counters are cleared for the next call.
+__device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w, uint32_t* out_flags) {
     const int lane = threadIdx.x & 31;
     const int k = p.k_use;
     uint32_t flags = p.row_flag[row];
@@ -651,15 +737,13 @@ __device__ void finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
         if (flags & FLAG_TIMEOUT) {
             p.next[row] = -1;
             atomicOr(p.status, flags);
-        } else if (exact) {
-            const int at = atomicAdd(s_xn, 1);
-            s_xrow[at] = row;
-            s_xflag[at] = flags;
         }
         if (p.row_flags) p.row_flags[row] = flags | ((exact && !(flags & FLAG_TIMEOUT)) ? FLAG_EXACT : 0u);
         p.row_cnt[row] = 0u;  // left clear for the next call on this workspace
         p.row_flag[row] = 0u;
     }
+    *out_flags = flags;
+    return exact && !(flags & FLAG_TIMEOUT);
 }
 
 // Rows of the exact replay need a whole CTA; the finish kernel's CTAs are
@@ -669,27 +753,56 @@ constexpr size_t F_REGION = F_WARP_AREA > REGION_BYTES ? F_WARP_AREA : REGION_BY
 constexpr size_t F_SMEM = (F_REGION + 15) / 16 * 16 + sizeof(Misc);
 static_assert(F_WARPS * 32 == NT, "the replay needs a CTA of NT threads");
 
-__global__ void __launch_bounds__(F_WARPS * 32) finish_rows_kernel(Params p) {
+// Three CTAs per SM (80 registers): the per-warp replays are latency-bound, so
+// more resident warps replay more rows at once.
+__global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) {
     extern __shared__ __align__(128) unsigned char fsmem[];
     __shared__ Ent s_heap[HEAP_SMEM_MAX];
     __shared__ int64_t s_xrow[F_WARPS];
     __shared__ uint32_t s_xflag[F_WARPS];
-    __shared__ int s_xn;
+    __shared__ int s_xn, s_wn;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     FinishWarpSmem& w = reinterpret_cast<FinishWarpSmem*>(fsmem)[warp];
     const int64_t row = (int64_t)blockIdx.x * F_WARPS + warp;
-    if (threadIdx.x == 0) s_xn = 0;
+    if (threadIdx.x == 0) s_xn = s_wn = 0;
+    MXS_PROF_BEGIN();
     csync();
-    if (row < p.rows) finish_row_warp(p, row, w, s_xrow, s_xflag, &s_xn);
+    uint32_t flags = 0u;
+    const bool need = row < p.rows && finish_row_warp(p, row, w, &flags);
+    const bool nan = (flags & FLAG_NAN) != 0;
+    if (lane == 0 && need && !nan) atomicAdd(&s_wn, 1);
     csync();
-    // the CTA replays the rows its warps handed over
+    // Several tie rows: each warp replays its own (rows with NaN excepted).
+    // One: the whole CTA replays it, which reads the row faster.
+    const bool by_warp = s_wn >= p.replay_warp_min;
+    if (by_warp && need && !nan) exact_row_warp(p, row, w);
+    if (lane == 0 && need && (nan || !by_warp)) {
+        const int at = atomicAdd(&s_xn, 1);
+        s_xrow[at] = row;
+        s_xflag[at] = flags;
+    }
+    csync();
     Misc& sm = *reinterpret_cast<Misc*>(fsmem + (F_REGION + 15) / 16 * 16);
     const int n = s_xn;
+    MXS_PROF_T0(tx);
     for (int i = 0; i < n; ++i)
         exact_row_t<true>(p, s_xrow[i], (s_xflag[i] & FLAG_NAN) ? 1 : 0, fsmem, sm, s_heap);
+    MXS_PROF_ADD(7, tx);
+    MXS_PROF_COUNT(6, n);
+    MXS_PROF_FLUSH();
 }
 
-
+#ifdef MXS_PROFILE
+// Phase counters of the finish kernel's CTA replays (profiling build only).
+extern "C" __attribute__((visibility("default"))) int mxs_prof_read_finish(unsigned long long* host, int clear) {
+    if (cudaMemcpyFromSymbol(host, g_mxs_prof, sizeof(g_mxs_prof)) != cudaSuccess) return -3;
+    if (clear) {
+        static unsigned long long zeros[PROF_CTAS][PROF_PHASES];
+        if (cudaMemcpyToSymbol(g_mxs_prof, zeros, sizeof(zeros)) != cudaSuccess) return -3;
+    }
+    return 0;
+}
+#endif
 
 size_t stream_smem_bytes() { return S_SMEM; }
 

@@ -32,7 +32,14 @@
 //           heap order of __heap_select + __sort_heap, not index order);
 //   mode 1: this file's own restatement of that heap process (Floyd build,
 //           hole sift-down to a leaf, then sift-up), which the CUDA kernels
-//           also implement; tests cross-check mode 1 against mode 0.
+//           also implement; tests cross-check mode 1 against mode 0;
+//   mode 2: mode 1 with each replacement of the root (select and sort phases)
+//           done top-down: the hole moves along the same child path but stops
+//           at the first child holding a value strictly greater than the new
+//           entry. While every value is ordered (no NaN) the heap property
+//           makes the path's values non-decreasing, so this leaves exactly the
+//           heap that the leaf-first descent plus sift-up leaves; the CUDA
+//           replays use it for rows without NaN. Rows with NaN take mode 1.
 //
 // Parity pin: the reference has no sampler tests or golden vectors. The pin is
 // oracle/_ref, which compiles the reference's own sampling block (sliced from
@@ -90,6 +97,19 @@ struct HeapRow {
         }
         sift_up(hole, top, v);
     }
+    // Top-down replacement of the root (mode 2): same child choice as place().
+    void place_top(int64_t len, int32_t v) {
+        int64_t hole = 0;
+        for (;;) {
+            int64_t c = 2 * hole + 1;
+            if (c >= len) break;
+            if (c + 1 < len && !before(h[c + 1], h[c])) c++;
+            if (before(h[c], v)) break;  // the child holds a strictly greater value
+            h[hole] = h[c];
+            hole = c;
+        }
+        h[hole] = v;
+    }
     void build(int64_t len) {
         if (len < 2) return;
         for (int64_t p = (len - 2) / 2;; --p) {
@@ -99,22 +119,31 @@ struct HeapRow {
     }
 };
 
-void restated_partial_sort(const float* x, int64_t vocab, int64_t k, int32_t* order) {
+void restated_partial_sort(const float* x, int64_t vocab, int64_t k, int32_t* order, bool top_down = false) {
     HeapRow hr{x, order};
+    if (top_down)
+        for (int64_t i = 0; i < vocab; ++i)
+            if (x[i] != x[i]) top_down = false;
     for (int64_t i = 0; i < vocab; ++i) order[i] = (int32_t)i;
     hr.build(k);
     for (int64_t i = k; i < vocab; ++i) {
         if (hr.before((int32_t)i, order[0])) {
             const int32_t v = order[i];
             order[i] = order[0];
-            hr.place(0, k, v);
+            if (top_down)
+                hr.place_top(k, v);
+            else
+                hr.place(0, k, v);
         }
     }
     for (int64_t len = k; len > 1;) {
         --len;
         const int32_t v = order[len];
         order[len] = order[0];
-        hr.place(0, len, v);
+        if (top_down)
+            hr.place_top(len, v);
+        else
+            hr.place(0, len, v);
     }
 }
 
@@ -149,7 +178,7 @@ int32_t sample_row(const float* x, int64_t vocab, double temperature, int top_k,
         std::partial_sort(order, order + k_use, order + vocab,
                           [&](int a, int b) { return (double)x[a] > (double)x[b]; });
     } else {
-        restated_partial_sort(x, vocab, k_use, order);
+        restated_partial_sort(x, vocab, k_use, order, mode == 2);
     }
     if (topk_idx) std::memcpy(topk_idx, order, sizeof(int32_t) * (size_t)k_use);
 
@@ -301,7 +330,7 @@ void mxs_oracle_topk_order(const float* x, int64_t vocab, int top_k, int mode, i
         std::partial_sort(order.begin(), order.begin() + k_use, order.end(),
                           [&](int a, int b) { return (double)x[a] > (double)x[b]; });
     } else {
-        restated_partial_sort(x, vocab, k_use, order.data());
+        restated_partial_sort(x, vocab, k_use, order.data(), mode == 2);
     }
     std::memcpy(out, order.data(), sizeof(int32_t) * (size_t)k_use);
 }

@@ -72,7 +72,7 @@ GOLDEN_CASES = load_golden()
 
 
 @pytest.mark.parametrize("c", GOLDEN_CASES, ids=[c["name"] for c in GOLDEN_CASES])
-@pytest.mark.parametrize("mode", [0, 1], ids=["stl", "restated"])
+@pytest.mark.parametrize("mode", [0, 1, 2], ids=["stl", "restated", "top_down"])
 def test_oracle_matches_reference_golden(c, mode):
     x = golden_logits(c)
     u = oracle_lib.uniforms(c["seed"], x.shape[0])
@@ -109,11 +109,30 @@ def test_heap_restatement_matches_std_partial_sort():
         np.testing.assert_array_equal(oracle_lib.topk_order(x, k, 0), oracle_lib.topk_order(x, k, 1))
 
 
+def test_top_down_replacement_matches_std_partial_sort():
+    """Mode 2 (the replacement the CUDA replays use on rows without NaN) against
+    the real std::partial_sort, on heavily tied rows and rows with NaN."""
+    rng = np.random.default_rng(17)
+    for trial in range(600):
+        V = int(rng.integers(1, 900))
+        k = int(rng.integers(0, min(V, 200) + 2))
+        q = float(rng.choice([0.25, 1.0, 4.0, 64.0]))
+        x = (np.round(rng.standard_normal(V) * q) / q).astype(np.float32)
+        if trial % 7 == 0:
+            x[rng.random(V) < 0.05] = -np.inf
+        if trial % 11 == 0:
+            x[rng.random(V) < 0.02] = np.nan
+        if trial % 13 == 0:
+            x = np.sort(x)  # increasing: every logit enters
+        np.testing.assert_array_equal(oracle_lib.topk_order(x, k, 0), oracle_lib.topk_order(x, k, 2), err_msg=str(trial))
+
+
 def test_known_tie_order():
     # 12 equal logits, k = 5: libstdc++'s heap leaves 3 4 1 0 2, not 0 1 2 3 4.
     x = np.zeros(12, np.float32)
     assert list(oracle_lib.topk_order(x, 5, 0)) == [3, 4, 1, 0, 2]
     assert list(oracle_lib.topk_order(x, 5, 1)) == [3, 4, 1, 0, 2]
+    assert list(oracle_lib.topk_order(x, 5, 2)) == [3, 4, 1, 0, 2]
 
 
 def test_injected_u_equals_discrete_distribution():

@@ -15,12 +15,14 @@ from test_oracle import GOLDEN_CASES, check_against_golden, golden_logits
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["split", "fused_ws", "block_sync"], autouse=True)
+@pytest.fixture(params=["split", "split_cta_replay", "fused_ws", "block_sync"], autouse=True)
 def kernel_variant(request, monkeypatch):
-    """Run every parity case on each kernel path: the three-kernel path
-    (stream -> finish -> exact, default for k <= 64), the one-launch
+    """Run every parity case on each kernel path: the two-kernel path
+    (stream -> finish, default for k <= 128) with its tie rows replayed one per
+    warp, the same with every tie row replayed by a whole CTA, the one-launch
     warp-specialised kernel, and the CTA-synchronous kernel."""
     monkeypatch.delenv("MXS_SAMPLER_BLOCK_PATH", raising=False)
+    monkeypatch.setenv("MXS_REPLAY_WARP_MIN", "9" if request.param == "split_cta_replay" else "1")
     if request.param == "fused_ws":
         monkeypatch.setenv("MXS_SAMPLER_PATH", "fused")
     elif request.param == "block_sync":
@@ -95,6 +97,19 @@ def test_config5_throughput_shapes(mxs, rows):
     assert_parity(x, 0.8, 50, u, got, name=f"c5 rows={rows}")
     # tie-free N(0, 2^2) rows must stay on the streaming path, not the replay
     assert ((got[3] & mxs.ROW_EXACT) != 0).sum() <= max(1, rows // 100)
+
+
+@pytest.mark.parametrize("k", [8, 50, 128])
+def test_bf16_rounded_rows_all_tied(mxs, k):
+    """Logits rounded to bf16 (a bf16 lm_head upcast to fp32) tie inside the
+    top-k of nearly every row, so the whole batch takes the exact replay."""
+    x = workloads.normal(400 + k, 96, workloads.V_QWEN, 2.0)
+    x = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    u = oracle_lib.uniforms(400 + k, x.shape[0])
+    got = run_gpu(mxs, x, 0.8, k, u)
+    assert_parity(x, 0.8, k, u, got, name=f"bf16 rows k={k}")
+    if k >= 50:
+        assert ((got[3] & mxs.ROW_EXACT) != 0).mean() > 0.9
 
 
 def test_ragged_vocab_strided_and_unaligned(mxs):
@@ -205,6 +220,6 @@ def test_ties_next_only_without_topk_outputs(mxs, kernel_variant, k):
         torch.cuda.synchronize()
         n0, _, _ = oracle_lib.oracle_sample(x, T, k, u)
         np.testing.assert_array_equal(nxt.cpu().numpy(), n0, err_msg=f"k={k} T={T}")
-        if kernel_variant == "split" and k >= 8 and T > 0:
+        if kernel_variant.startswith("split") and k >= 8 and T > 0:
             # these rows have ties, but some draws miss the tied positions
             assert (flags.cpu().numpy() & mxs.ROW_EXACT).mean() < 0.99
