@@ -73,7 +73,7 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 struct Plan {
     int k_use = 1;
     int S = 1, tpc = 1, grid = 1, outcap = 0;
-    bool split = false;  // three-kernel path (stream -> finish -> exact)
+    bool split = false;  // two-kernel path (stream -> finish, which also replays tie rows)
     size_t off_rcand = 0, off_rcnt = 0, off_rflag = 0, zero_bytes = 0;
     int64_t units = 0;
     size_t off_counter = 0, off_state = 0, off_status = 0, off_ccount = 0, off_cand = 0, off_heap = 0,
@@ -86,7 +86,7 @@ int clamp_k(int top_k, int64_t vocab) {
     return (int)k;
 }
 
-// The three-kernel path takes sampling calls with k <= KSPLIT on 16-byte aligned
+// The two-kernel path takes sampling calls with k <= KSPLIT on 16-byte aligned
 // rows. MXS_SAMPLER_PATH selects another kernel for every call ("fused": the
 // one-launch warp-specialised kernel, "block": the CTA-synchronous one); the
 // parity tests run all three. MXS_SAMPLER_BLOCK_PATH=1 is the older spelling of
@@ -227,7 +227,7 @@ int launch(Params& p, const Plan& pl, cudaStream_t stream, int sms = 148, cudaEv
         const bool clean = lib_ws_owner && lib_ws_owner->clean_rows == p.rows && lib_ws_owner->clean_off == pl.off_rcnt;
         if (lib_ws_owner) lib_ws_owner->clean_rows = -1;
         if (!clean && cudaMemsetAsync(p.row_cnt, 0, pl.zero_bytes, stream) != cudaSuccess) return MXS_ERR_CUDA;
-        if (mxs::stream_path_launch(p, pl.grid, sms, stream, ev0, ev1) != cudaSuccess) return MXS_ERR_CUDA;
+        if (mxs::stream_path_launch(p, pl.grid, stream, ev0, ev1) != cudaSuccess) return MXS_ERR_CUDA;
         if (lib_ws_owner) {
             lib_ws_owner->clean_rows = p.rows;
             lib_ws_owner->clean_off = pl.off_rcnt;

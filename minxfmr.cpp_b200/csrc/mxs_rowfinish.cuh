@@ -263,7 +263,7 @@ __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int na
 
 // Exact replay of the reference's partial_sort heap process over row `row`,
 // then the draw (see exact_row_t).
-// The heap of a small k lives at the start of `region` (exact_rows_kernel
+// The heap of a small k lives at the start of `region` (finish_rows_kernel
 // passes a static __shared__ array to exact_row_t directly instead).
 __device__ __forceinline__ void exact_row(const Params& p, int64_t row, int nan_state, unsigned char* region,
                                           Misc& sm) {

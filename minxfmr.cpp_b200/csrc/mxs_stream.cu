@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
 }
 
 // One warp per row: select, register sort, tie check, draw; rows that need the
-// exact replay go to the exact kernel's list.
+// exact replay are replayed by the same kernel afterwards.
 constexpr int F_WARPS = 8;
 struct FinishWarpSmem {
     uint32_t keys[FCAP];
@@ -814,7 +814,7 @@ cudaError_t stream_path_configure(int* blocks_per_sm) {
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, stream_select_kernel, NT_WS, S_SMEM);
 }
 
-cudaError_t stream_path_launch(const Params& p, int grid, int exact_grid, cudaStream_t stream, cudaEvent_t ev_start,
+cudaError_t stream_path_launch(const Params& p, int grid, cudaStream_t stream, cudaEvent_t ev_start,
                                cudaEvent_t ev_stop) {
     if (ev_start) cudaEventRecord(ev_start, stream);
     stream_select_kernel<<<grid, NT_WS, S_SMEM, stream>>>(p);
