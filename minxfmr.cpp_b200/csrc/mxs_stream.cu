@@ -292,6 +292,15 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 wseed = bound_of(own);
                 lkey = (lane < m) ? sorted1 : 0u;
                 publish();
+                // Once every consumer warp has published its first-tile m-th
+                // key, their minimum bounds the unit's k-th largest: filter the
+                // first tile against it rather than this warp's own seed alone
+                // (about 8 logits per slice pass instead of about k).
+                csync();
+                uint32_t mn = (lane < NWARPS) ? *reinterpret_cast<volatile uint32_t*>(&us.pub[lane]) : 0xFFFFFFFFu;
+#pragma unroll
+                for (int d = 16; d > 0; d >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, d));
+                if (mn) wseed = fmaxf(wseed, bound_of(mn));
             }
             const float thr = bound();
             if (!stopped && __any_sync(0xffffffffu, mxn >= thr)) {
