@@ -45,6 +45,16 @@ constexpr size_t S_WBUF = size_t(NWARPS) * SW_CAP * 8;
 constexpr size_t S_HIST = size_t(NWARPS) * 256 * 4;
 constexpr size_t S_SMEM = S_RING + S_WBUF + S_HIST + sizeof(StreamSmem);
 
+// Counters of the profiling build: lane 0 of each warp adds to the CTA's totals.
+#ifdef MXS_PROFILE
+#define MXS_WCOUNT(ph, n)                                                                   \
+    do {                                                                                    \
+        if ((threadIdx.x & 31) == 0) atomicAdd(&mxs::s_mxs_prof[ph], (unsigned long long)(n)); \
+    } while (0)
+#else
+#define MXS_WCOUNT(ph, n) (void)0
+#endif
+
 // Publish this warp's m-th largest key; the smallest value every warp has
 // published bounds the unit's k-th largest from below (the warps' slices are
 // disjoint and NWARPS * m >= k). Until all have published, a warp holding k
@@ -125,6 +135,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
         }
         fence_mbar_init();
     }
+    MXS_PROF_BEGIN();
     __syncthreads();
 
     if (warp == NWARPS) {  // producer
@@ -321,6 +332,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 uint32_t mm = pass_bits(thr);
                 int cc = __popc(mm);
                 int incl, tot;
+                MXS_WCOUNT(2, 1);
                 if (!__any_sync(0xffffffffu, cc > 1)) {  // usual case: at most one per lane
                     const uint32_t one = __ballot_sync(0xffffffffu, cc != 0);
                     incl = __popc(one & ((2u << lane) - 1u));
@@ -329,7 +341,9 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     incl = warp_incl_scan(cc);
                     tot = __shfl_sync(0xffffffffu, incl, 31);
                 }
+                MXS_WCOUNT(t == 0 ? 0 : 1, tot);
                 if (wcnt + tot > SW_CAP) {
+                    MXS_WCOUNT(3, 1);
                     // Does not fit (a loose bound, e.g. on the first tile): append
                     // in rounds of at most two logits per lane (64 per warp), and
                     // before each round make room: drop what the shared bound
@@ -438,6 +452,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     }
                 }
                 wcnt += tot;
+                if (grows && t > 0) MXS_WCOUNT(4, 1);
                 if (grows && t > 0) publish();
                 if (wcnt > SW_CAP - 40)
                     wcnt = warp_compact_ge(wk, wi, wcnt, *reinterpret_cast<volatile uint32_t*>(&us.thr_key));
@@ -453,6 +468,8 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
         // Leave the unit: append the survivors (>= the bound now) to the row's list.
         const uint32_t T = *reinterpret_cast<volatile uint32_t*>(&us.thr_key);
         const int n = warp_compact_ge(wk, wi, wcnt, T);
+        MXS_WCOUNT(5, n);
+        if (warp == 0) MXS_WCOUNT(6, 1);
         uint32_t base = 0;
         if (lane == 0 && n) base = atomicAdd(&p.row_cnt[row], (uint32_t)n);
         base = __shfl_sync(0xffffffffu, base, 0);
@@ -478,6 +495,10 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
         }
         __syncwarp();
     }
+#ifdef MXS_PROFILE
+    csync();  // consumers only: the counters are complete
+    MXS_PROF_FLUSH();
+#endif
 }
 
 // One warp per row: select, register sort, tie check, draw; rows that need the
