@@ -51,6 +51,7 @@ extern "C" {
 #define MXS_ERR_TIMEOUT (-4)   /* a bounded device wait gave up (see mxs_get_status) */
 #define MXS_ERR_NO_DEVICE (-5) /* no sm_100 device current */
 #define MXS_ERR_WORKSPACE (-6) /* caller workspace too small or misaligned */
+#define MXS_ERR_COMM (-7)      /* NCCL not loaded in the process, or a collective failed */
 
 /* Per-row flag bits written to d_row_flags (optional). */
 #define MXS_ROW_EXACT 1u    /* the row had ties (or NaNs) and was resolved by the exact heap replay */
@@ -134,6 +135,40 @@ MXS_API int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count
                      int nshards, int cap, int64_t rows, int64_t vocab, double temperature, int top_k,
                      double top_p, double min_p, const double* d_u, int32_t* d_next, int32_t* d_topk_idx,
                      double* d_topk_prob, uint32_t* d_row_flags, void* stream);
+
+/*
+ * Row-sharded sampling (no collective; rows are independent): rank `rank` of
+ * `world` takes rows [rank*P, min(global_rows, (rank+1)*P)), P = ceil(global_rows
+ * / world), of a batch split over the ranks. d_local_logits holds those rows
+ * (row i at d_local_logits + i*ld); d_u_global holds every row's uniform (the
+ * call reads this rank's range); the outputs are this rank's rows. The number of
+ * local rows is written to *local_rows (nullable). Otherwise as
+ * mxs_sample_topk_ex with the library workspace. The sharded form of
+ * src/api/minxfmr.cpp:2091-2171 over a batch.
+ */
+MXS_API int mxs_sample_rowsharded(const float* d_local_logits, int64_t global_rows, int rank, int world,
+                                  int64_t vocab, int64_t ld, double temperature, int top_k, double top_p,
+                                  double min_p, const double* d_u_global, int32_t* d_next, int32_t* d_topk_idx,
+                                  double* d_topk_prob, uint32_t* d_row_flags, int64_t* local_rows, void* stream);
+
+/*
+ * Vocab-sharded sampling in one call per rank (collective over nccl_comm, an
+ * ncclComm_t of the NCCL the process has loaded; world = its size). Every rank
+ * passes the same rows: its column shard [rank*shard_cols, (rank+1)*shard_cols)
+ * of a vocabulary of world*shard_cols, and the same d_u. Runs
+ * mxs_shard_candidates, one NCCL all-gather group of the lists, and
+ * mxs_merge_sample on the given stream; rows whose merged lists show a tie are
+ * then gathered whole (one more all-gather) and sampled as full rows, so every
+ * rank ends with the same outputs for every row, equal to mxs_sample_topk_ex
+ * on the full rows. Synchronises the stream once, to learn how many rows need
+ * the full-row pass. d_row_flags (nullable) gets MXS_ROW_EXACT on those rows.
+ * top_k is at most 2048 here (as mxs_merge_sample). Returns MXS_ERR_COMM when
+ * NCCL is not loaded or a collective fails.
+ */
+MXS_API int mxs_sample_vocabsharded(const float* d_shard_logits, int64_t rows, int64_t shard_cols, int64_t ld,
+                                    double temperature, int top_k, double top_p, double min_p, const double* d_u,
+                                    int32_t* d_next, int32_t* d_topk_idx, double* d_topk_prob,
+                                    uint32_t* d_row_flags, void* nccl_comm, void* stream);
 
 /*
  * Measurement hook (no counterpart in the reference): when set, the next

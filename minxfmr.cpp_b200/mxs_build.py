@@ -14,7 +14,7 @@ OUT_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(OUT_DIR, "libmxs.so")
 # phase-timer build (-DMXS_PROFILE) for kernel analysis; never loaded by the product path
 PROF_LIB = os.path.join(OUT_DIR, "libmxs_prof.so")
-SOURCES = ["mxs_sampler.cu", "mxs_stream.cu", "mxs_api.cu", "mxs_noalloc.cu"]
+SOURCES = ["mxs_sampler.cu", "mxs_stream.cu", "mxs_api.cu", "mxs_noalloc.cu", "mxs_multi.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -22,7 +22,7 @@ FLAGS = [
     # every double operation of the draw must round exactly as the reference's
     "-fmad=false", "-prec-div=true", "-prec-sqrt=true",
     "-Xcompiler", "-fPIC,-fvisibility=hidden",
-    "-shared", "-cudart", "static",
+    "-shared", "-cudart", "static", "-ldl",
 ]
 
 

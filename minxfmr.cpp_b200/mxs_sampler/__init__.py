@@ -26,6 +26,7 @@ MXS_ERR_CUDA = -3
 MXS_ERR_TIMEOUT = -4
 MXS_ERR_NO_DEVICE = -5
 MXS_ERR_WORKSPACE = -6
+MXS_ERR_COMM = -7
 
 ROW_EXACT = 1
 ROW_NAN = 2
@@ -36,7 +37,8 @@ ROW_TIMEOUT = 8
 EXPORTS = (
     "mxs_sample_topk", "mxs_sample_topk_ex", "mxs_workspace_size", "mxs_workspace_init",
     "mxs_sample_topk_host", "mxs_shard_candidates", "mxs_merge_sample", "mxs_get_status",
-    "mxs_version", "mxs_sample_topk_noalloc", "mxs_set_profile_events",
+    "mxs_version", "mxs_sample_topk_noalloc", "mxs_set_profile_events", "mxs_sample_rowsharded",
+    "mxs_sample_vocabsharded",
 )
 
 _P = ctypes.c_void_p
@@ -56,6 +58,9 @@ _SIGS = {
     "mxs_get_status": [ctypes.POINTER(ctypes.c_uint32), _I],
     "mxs_set_profile_events": [_P, _P],
     "mxs_sample_topk_noalloc": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _P],
+    "mxs_sample_rowsharded": [_P, _I64, _I, _I, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P,
+                              ctypes.POINTER(_I64), _P],
+    "mxs_sample_vocabsharded": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _P, _P],
 }
 
 _lib = None
@@ -254,6 +259,60 @@ def merge_sample(cand_all, count_all, flags_all, vocab, temperature, top_k, u, t
                                      _ptr(prob), _ptr(rflg), _stream(stream))
     _check("mxs_merge_sample", rc)
     return nxt, idx, prob, rflg
+
+
+def sample_rowsharded(local_logits, global_rows, rank, world, temperature, top_k, u_global, top_p=1.0,
+                      min_p=0.0, stream=None):
+    """This rank's rows of a batch split over `world` ranks (no collective):
+    local_logits [local_rows, vocab], u_global [global_rows] float64. Returns
+    (next, topk_idx, topk_prob, row_flags) for the local rows."""
+    _need_cuda(local_logits, "local_logits", torch.float32)
+    _need_cuda(u_global, "u_global", torch.float64)
+    rows, vocab = local_logits.shape
+    per = (global_rows + world - 1) // world
+    want = max(0, min(global_rows, (rank + 1) * per) - min(global_rows, rank * per))
+    if rows != want:
+        raise ValueError(f"rank {rank} of {world} holds {want} of {global_rows} rows, got {rows}")
+    dev = local_logits.device
+    k = k_use(int(top_k), vocab)
+    nxt = torch.empty(rows, dtype=torch.int32, device=dev)
+    idx = torch.empty((rows, k), dtype=torch.int32, device=dev)
+    prob = torch.empty((rows, k), dtype=torch.float64, device=dev)
+    flg = torch.empty(rows, dtype=torch.int32, device=dev)
+    n = ctypes.c_int64(0)
+    with torch.cuda.device(dev):
+        rc = load().mxs_sample_rowsharded(_ptr(local_logits), int(global_rows), int(rank), int(world), vocab,
+                                          local_logits.stride(0), float(temperature), int(top_k), float(top_p),
+                                          float(min_p), _ptr(u_global), _ptr(nxt), _ptr(idx), _ptr(prob), _ptr(flg),
+                                          ctypes.byref(n), _stream(stream))
+    _check("mxs_sample_rowsharded", rc)
+    return nxt, idx, prob, flg
+
+
+def sample_vocabsharded(shard_logits, temperature, top_k, u, comm, top_p=1.0, min_p=0.0, stream=None):
+    """One collective call per rank over an NCCL communicator (an integer
+    ncclComm_t, e.g. from mxs_sampler.nccl.comm_init_rank): shard_logits is this
+    rank's [rows, vocab / world] column shard, u the [rows] uniforms (the same on
+    every rank). Returns (next, topk_idx, topk_prob, row_flags) for every row,
+    the same on every rank."""
+    _need_cuda(shard_logits, "shard_logits", torch.float32)
+    _need_cuda(u, "u", torch.float64)
+    rows, cols = shard_logits.shape
+    from . import nccl as _nccl
+    vocab = cols * _nccl.comm_count(comm)
+    dev = shard_logits.device
+    k = k_use(int(top_k), vocab)
+    nxt = torch.empty(rows, dtype=torch.int32, device=dev)
+    idx = torch.empty((rows, k), dtype=torch.int32, device=dev)
+    prob = torch.empty((rows, k), dtype=torch.float64, device=dev)
+    flg = torch.empty(rows, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        rc = load().mxs_sample_vocabsharded(_ptr(shard_logits), rows, cols, shard_logits.stride(0),
+                                            float(temperature), int(top_k), float(top_p), float(min_p), _ptr(u),
+                                            _ptr(nxt), _ptr(idx), _ptr(prob), _ptr(flg), ctypes.c_void_p(comm),
+                                            _stream(stream))
+    _check("mxs_sample_vocabsharded", rc)
+    return nxt, idx, prob, flg
 
 
 def set_profile_events(start=None, stop=None):

@@ -60,6 +60,26 @@ def test_invalid_arguments_rejected_without_device(lib):
         mxs_sampler.MXS_ERR_INVALID
 
 
+
+def test_sharded_entry_points_check_arguments_without_device(lib):
+    P = ctypes.c_void_p
+    n = ctypes.c_int64(-1)
+    # rank outside [0, world), world <= 0
+    assert lib.mxs_sample_rowsharded(P(16), 10, 2, 2, 100, 100, 1.0, 5, 1.0, 0.0, P(16), P(16), None, None, None,
+                                     ctypes.byref(n), None) == mxs_sampler.MXS_ERR_INVALID
+    assert lib.mxs_sample_rowsharded(P(16), 10, 0, 0, 100, 100, 1.0, 5, 1.0, 0.0, P(16), P(16), None, None, None,
+                                     ctypes.byref(n), None) == mxs_sampler.MXS_ERR_INVALID
+    # a rank whose range is empty (10 rows over 8 ranks: 2 per rank, rank 7 has none) succeeds with 0 rows
+    assert lib.mxs_sample_rowsharded(None, 10, 7, 8, 100, 100, 1.0, 5, 1.0, 0.0, None, None, None, None, None,
+                                     ctypes.byref(n), None) == mxs_sampler.MXS_OK
+    assert n.value == 0
+    # no communicator, ld < shard columns
+    assert lib.mxs_sample_vocabsharded(P(16), 4, 100, 100, 1.0, 5, 1.0, 0.0, P(16), P(16), None, None, None, None,
+                                       None) == mxs_sampler.MXS_ERR_INVALID
+    assert lib.mxs_sample_vocabsharded(P(16), 4, 100, 50, 1.0, 5, 1.0, 0.0, P(16), P(16), None, None, None, P(16),
+                                       None) == mxs_sampler.MXS_ERR_INVALID
+
+
 def test_no_cpu_fallback_without_gpu(lib):
     import torch
     if torch.cuda.is_available():

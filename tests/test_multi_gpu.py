@@ -2,7 +2,9 @@
 
 - vocab-sharded sampling: each rank holds one column shard; candidate lists are
   all-gathered and merged on every rank; the result must equal the oracle's on
-  the full rows, on every rank, tie rows included;
+  the full rows, on every rank, tie rows included. Run twice: through
+  torch.distributed (mxs_sampler.dist) and through the C ABI's one-call
+  mxs_sample_vocabsharded over an NCCL communicator;
 - row-sharded bench: bench.py under torchrun prints one JSON line."""
 import json
 import os
@@ -48,9 +50,26 @@ torch.cuda.synchronize()
 n0, i0, p0 = oracle_lib.oracle_sample(x, T, k, u)
 ok = bool((nxt.cpu().numpy() == n0).all() and (idx.cpu().numpy() == i0).all()
           and np.allclose(prob.cpu().numpy(), p0, rtol=1e-6, atol=0))
-print(json.dumps({"rank": rank, "ok": ok, "exact_rows": int((fl.cpu().numpy() & 1).sum())}), flush=True)
+# the same through the C ABI: one mxs_sample_vocabsharded call per rank over an NCCL communicator
+import mxs_sampler
+from mxs_sampler import nccl
+obj = [nccl.get_unique_id() if rank == 0 else None]
+dist.broadcast_object_list(obj, 0)
+comm = nccl.comm_init_rank(world, obj[0], rank)
+ok_abi = True
+for xx in (x, torch.from_numpy(workloads.normal(78, 48, V, 2.0)).bfloat16().float().numpy()):
+    uu = oracle_lib.uniforms(78, xx.shape[0])
+    sh = torch.from_numpy(xx[:, rank * cols:(rank + 1) * cols].copy()).cuda()
+    n2, i2, p2, f2 = mxs_sampler.sample_vocabsharded(sh, T, k, torch.from_numpy(uu).cuda(), comm)
+    torch.cuda.synchronize()
+    m0, j0, q0 = oracle_lib.oracle_sample(xx, T, k, uu)
+    ok_abi = ok_abi and bool((n2.cpu().numpy() == m0).all() and (i2.cpu().numpy() == j0).all()
+                             and np.allclose(p2.cpu().numpy(), q0, rtol=1e-6, atol=0))
+nccl.comm_destroy(comm)
+print(json.dumps({"rank": rank, "ok": ok, "ok_abi": ok_abi, "exact_rows": int((fl.cpu().numpy() & 1).sum())}),
+      flush=True)
 dist.destroy_process_group()
-sys.exit(0 if ok else 3)
+sys.exit(0 if (ok and ok_abi) else 3)
 '''
 
 
@@ -71,7 +90,7 @@ def test_vocab_sharded_nccl_two_gpus():
         assert p.returncode == 0, o[-3000:]
         line = [l for l in o.splitlines() if l.startswith("{")][-1]
         d = json.loads(line)
-        assert d["ok"] and d["exact_rows"] >= 2
+        assert d["ok"] and d["ok_abi"] and d["exact_rows"] >= 2
 
 
 def test_row_sharded_bench_two_gpus():
