@@ -162,8 +162,8 @@ MXS_API int mxs_sample_rowsharded(const float* d_local_logits, int64_t global_ro
  * rank ends with the same outputs for every row, equal to mxs_sample_topk_ex
  * on the full rows. Synchronises the stream once, to learn how many rows need
  * the full-row pass. d_row_flags (nullable) gets MXS_ROW_EXACT on those rows.
- * top_k is at most 2048 here (as mxs_merge_sample). Returns MXS_ERR_COMM when
- * NCCL is not loaded or a collective fails.
+ * Above top_k = 2048 (the merge's limit) every row takes the full-row pass.
+ * Returns MXS_ERR_COMM when NCCL is not loaded or a collective fails.
  */
 MXS_API int mxs_sample_vocabsharded(const float* d_shard_logits, int64_t rows, int64_t shard_cols, int64_t ld,
                                     double temperature, int top_k, double top_p, double min_p, const double* d_u,

@@ -159,6 +159,15 @@ __global__ void scatter_full_results(const int32_t* list, int64_t i0, int64_t n,
     }
 }
 
+__global__ void fill_flags(uint32_t* flags, int64_t rows, uint32_t v) {
+    for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < rows; r += (int64_t)gridDim.x * blockDim.x)
+        flags[r] = v;
+}
+
+// The merge keeps at most this many survivors per row (mxs_merge_sample's
+// limit); above it every row takes the full-row pass.
+constexpr int MERGE_K_MAX = 2048;
+
 int grid_for(int64_t total) { return (int)std::min<int64_t>((total + 255) / 256, 148 * 8); }
 
 int clamp_k(int top_k, int64_t vocab) {
@@ -226,21 +235,26 @@ int mxs_sample_vocabsharded(const float* d_shard_logits, int64_t rows, int64_t s
     int32_t* list = static_cast<int32_t*>(b[B_LIST].p);
     uint32_t* list_count = reinterpret_cast<uint32_t*>(list + rows);
 
-    // 1. this shard's candidate lists
-    rc = mxs_shard_candidates(d_shard_logits, rows, shard_cols, ld, (int64_t)rank * shard_cols, top_k, cap, cand,
-                              cnt, flg, stream);
-    if (rc) return rc;
-    // 2. every shard's lists on every rank, as [world][rows][cap]
-    if (f.group_start() != ncclSuccess) return MXS_ERR_COMM;
-    ncclResult_t r1 = f.all_gather(cand, cand_all, (size_t)rows * cap, ncclUint64, comm, st);
-    ncclResult_t r2 = f.all_gather(cnt, cnt_all, (size_t)rows, ncclUint32, comm, st);
-    ncclResult_t r3 = f.all_gather(flg, flg_all, (size_t)rows, ncclUint32, comm, st);
-    if (f.group_end() != ncclSuccess || r1 != ncclSuccess || r2 != ncclSuccess || r3 != ncclSuccess)
-        return MXS_ERR_COMM;
-    // 3. merge and draw (identical on every rank)
-    rc = mxs_merge_sample(cand_all, cnt_all, flg_all, world, cap, rows, vocab, temperature, top_k, top_p, min_p, d_u,
-                          d_next, d_topk_idx, d_topk_prob, rflags, stream);
-    if (rc) return rc;
+    if (k_use > MERGE_K_MAX) {
+        fill_flags<<<grid_for(rows), 256, 0, st>>>(rflags, rows, MXS_ROW_EXACT);
+        if (cudaGetLastError() != cudaSuccess) return MXS_ERR_CUDA;
+    } else {
+        // 1. this shard's candidate lists
+        rc = mxs_shard_candidates(d_shard_logits, rows, shard_cols, ld, (int64_t)rank * shard_cols, top_k, cap, cand,
+                                  cnt, flg, stream);
+        if (rc) return rc;
+        // 2. every shard's lists on every rank, as [world][rows][cap]
+        if (f.group_start() != ncclSuccess) return MXS_ERR_COMM;
+        ncclResult_t r1 = f.all_gather(cand, cand_all, (size_t)rows * cap, ncclUint64, comm, st);
+        ncclResult_t r2 = f.all_gather(cnt, cnt_all, (size_t)rows, ncclUint32, comm, st);
+        ncclResult_t r3 = f.all_gather(flg, flg_all, (size_t)rows, ncclUint32, comm, st);
+        if (f.group_end() != ncclSuccess || r1 != ncclSuccess || r2 != ncclSuccess || r3 != ncclSuccess)
+            return MXS_ERR_COMM;
+        // 3. merge and draw (identical on every rank)
+        rc = mxs_merge_sample(cand_all, cnt_all, flg_all, world, cap, rows, vocab, temperature, top_k, top_p, min_p, d_u,
+                              d_next, d_topk_idx, d_topk_prob, rflags, stream);
+        if (rc) return rc;
+    }
     // 4. rows the merge handed back: gather them whole and sample them again
     list_exact_rows<<<1, 1024, 0, st>>>(rflags, rows, list, list_count);
     if (cudaGetLastError() != cudaSuccess) return MXS_ERR_CUDA;

@@ -80,3 +80,12 @@ def test_rowsharded_ranges_equal_one_call(mxs, world):
     assert torch.equal(torch.cat([g[0] for g in got]), n0)
     assert torch.equal(torch.cat([g[1] for g in got]), i0)
     assert torch.equal(torch.cat([g[2] for g in got]), p0)
+
+
+def test_vocabsharded_one_rank_k_above_merge_limit(mxs, comm1):
+    """top_k > 2048: every row goes to the full-row pass."""
+    x = np.round(workloads.normal(540, 6, 9000, 1.0) * 32) / 32
+    x = x.astype(np.float32)
+    u = oracle_lib.uniforms(540, 6)
+    fl = _vocab_case(mxs, comm1, x, 1.0, 3000, u)
+    assert (fl & mxs.ROW_EXACT).all()
