@@ -52,7 +52,8 @@ def get_unique_id():
     """128 bytes that every rank passes to comm_init_rank."""
     uid = _UniqueId()
     _check("ncclGetUniqueId", _nccl().ncclGetUniqueId(ctypes.byref(uid)))
-    return bytes(uid.internal)
+    # all 128 bytes (reading the c_char field would stop at its first zero byte)
+    return ctypes.string_at(ctypes.addressof(uid), 128)
 
 
 def comm_init_rank(world, uid, rank):
