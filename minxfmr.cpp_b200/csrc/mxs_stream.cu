@@ -700,8 +700,61 @@ __device__ void exact_row_warp(const Params& p, int64_t row, FinishWarpSmem& w) 
 
 // One warp finishes row `row`; returns true (in every lane) when the row needs
 // the replay. The row's counters are cleared for the next call.
+// The k-th largest of keys[0, n), n <= FCAP, for one warp: the keys stay in
+// registers (FCAP / 32 per lane) and the answer is built from the top bit
+// down, one bit per step, counting with a warp reduction. Same result as
+// warp_select_kth, without its shared-memory histogram passes.
+__device__ __forceinline__ uint32_t warp_select_kth_small(const uint32_t* keys, int n, int k) {
+    constexpr int PER = FCAP / 32;
+    const int lane = threadIdx.x & 31;
+    uint32_t kv[PER];
+    uint32_t a = ~0u, o = 0u;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int i = lane + 32 * j;
+        kv[j] = i < n ? keys[i] : 0u;
+        if (i < n) {
+            a &= kv[j];
+            o |= kv[j];
+        }
+    }
+    a = __reduce_and_sync(0xffffffffu, a);
+    o = __reduce_or_sync(0xffffffffu, o);
+    if (a == o) return a;
+    const int hi = 31 - __clz(a ^ o);
+    uint32_t mask = ~((2u << hi) - 1u);  // bits above hi: the same in every key
+    uint32_t prefix = a & mask;
+    unsigned krem = (unsigned)k;
+#pragma unroll 1
+    for (int b = hi; b >= 0; --b) {
+        const uint32_t tm = mask | (1u << b), tc = prefix | (1u << b);
+        unsigned c = 0;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) c += (lane + 32 * j < n && (kv[j] & tm) == tc) ? 1u : 0u;
+        c = __reduce_add_sync(0xffffffffu, c);
+        if (c >= krem)
+            prefix = tc;
+        else
+            krem -= c;
+        mask = tm;
+    }
+    return prefix;
+}
+
+#ifdef MXS_PROFILE
+// Phase clocks of row 0's finish warp (profiling build): list, select, sort + draw,
+// list length, in-loop selections.
+__device__ unsigned long long g_fin_prof[8];
+#define MXS_FIN_T(v) long long v = clock64()
+#define MXS_FIN_ADD(i, x) do { if (row == 0 && lane == 0) atomicAdd(&g_fin_prof[i], (unsigned long long)(x)); } while (0)
+#else
+#define MXS_FIN_T(v) (void)0
+#define MXS_FIN_ADD(i, x) (void)0
+#endif
+
 __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w, uint32_t* out_flags) {
     const int lane = threadIdx.x & 31;
+    MXS_FIN_T(f0);
     const int k = p.k_use;
     uint32_t flags = p.row_flag[row];
     const uint32_t cnt_all = p.row_cnt[row];
@@ -715,28 +768,33 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
         const uint32_t lt = (1u << lane) - 1u;
         int cnt = 0;
         uint32_t bound = 0u;
-        for (int i0 = 0; i0 < (int)cnt_all; i0 += 32) {
-            const int i = i0 + lane;
-            uint64_t v = 0;
-            bool take = false;
-            if (i < (int)cnt_all) {
-                v = src[i];
-                take = (uint32_t)(v >> 32) >= bound;
+        // 256 entries per load round trip (8 per lane in flight).
+        for (int i0 = 0; i0 < (int)cnt_all && !exact; i0 += 256) {
+            uint64_t vv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + 32 * j + lane;
+                vv[j] = i < (int)cnt_all ? src[i] : 0ull;
             }
-            const uint32_t bal = __ballot_sync(0xffffffffu, take);
-            if (take) {
-                const int pos = cnt + __popc(bal & lt);
-                w.keys[pos] = (uint32_t)(v >> 32);
-                w.idx[pos] = (int32_t)(uint32_t)v;
-            }
-            cnt += __popc(bal);
-            __syncwarp();
-            if (cnt > FCAP - 32) {
-                bound = warp_select_kth(w.keys, cnt, k, w.hist);
-                cnt = warp_compact_ge(w.keys, w.idx, cnt, bound);
-                if (cnt > FCAP - 32) {  // massive ties
-                    exact = true;
-                    break;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (exact || i0 + 32 * j >= (int)cnt_all) break;
+                const int i = i0 + 32 * j + lane;
+                const uint64_t v = vv[j];
+                const bool take = i < (int)cnt_all && (uint32_t)(v >> 32) >= bound;
+                const uint32_t bal = __ballot_sync(0xffffffffu, take);
+                if (take) {
+                    const int pos = cnt + __popc(bal & lt);
+                    w.keys[pos] = (uint32_t)(v >> 32);
+                    w.idx[pos] = (int32_t)(uint32_t)v;
+                }
+                cnt += __popc(bal);
+                __syncwarp();
+                if (cnt > FCAP - 32) {
+                    MXS_FIN_ADD(7, 1);
+                    bound = warp_select_kth_small(w.keys, cnt, k);
+                    cnt = warp_compact_ge(w.keys, w.idx, cnt, bound);
+                    if (cnt > FCAP - 32) exact = true;  // massive ties
                 }
             }
         }
@@ -745,9 +803,12 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
         // probabilities and their running sums depend only on the values by
         // position, so without a requested top-k list the draw is exact unless
         // it lands on a tied position; only then does the row need the replay.
+        MXS_FIN_T(f1);
+        MXS_FIN_ADD(0, f1 - f0);
+        MXS_FIN_ADD(6, cnt_all);
         bool tie = false;
         if (!exact && cnt > k) {
-            const uint32_t kth = warp_select_kth(w.keys, cnt, k, w.hist);
+            const uint32_t kth = warp_select_kth_small(w.keys, cnt, k);
             cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
             if (cnt != k) {  // a tie straddles the cut
                 tie = true;
@@ -756,12 +817,16 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
         } else if (!exact && cnt < k) {
             exact = true;
         }
+        MXS_FIN_T(f2);
+        MXS_FIN_ADD(1, f2 - f1);
         if (!exact) {
             if (cnt <= 64)
                 exact = finish_sorted<2>(p, row, w, cnt, k, tie, lane);
             else
                 exact = finish_sorted<4>(p, row, w, cnt, k, tie, lane);
         }
+        MXS_FIN_T(f3);
+        MXS_FIN_ADD(2, f3 - f2);
     }
     if (lane == 0) {
         if (flags & FLAG_TIMEOUT) {
@@ -823,6 +888,14 @@ __global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) 
 }
 
 #ifdef MXS_PROFILE
+extern "C" __attribute__((visibility("default"))) int mxs_prof_read_fin(unsigned long long* host, int clear) {
+    if (cudaMemcpyFromSymbol(host, g_fin_prof, sizeof(g_fin_prof)) != cudaSuccess) return -3;
+    if (clear) {
+        static unsigned long long zeros[8];
+        if (cudaMemcpyToSymbol(g_fin_prof, zeros, sizeof(zeros)) != cudaSuccess) return -3;
+    }
+    return 0;
+}
 // Phase counters of the finish kernel's CTA replays (profiling build only).
 extern "C" __attribute__((visibility("default"))) int mxs_prof_read_finish(unsigned long long* host, int clear) {
     if (cudaMemcpyFromSymbol(host, g_mxs_prof, sizeof(g_mxs_prof)) != cudaSuccess) return -3;
