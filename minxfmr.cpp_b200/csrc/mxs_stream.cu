@@ -702,7 +702,7 @@ __device__ void exact_row_warp(const Params& p, int64_t row, FinishWarpSmem& w) 
 // the replay. The row's counters are cleared for the next call.
 // The k-th largest of keys[0, n), n <= FCAP, for one warp: the keys stay in
 // registers (FCAP / 32 per lane) and the answer is built from the top bit
-// down, one bit per step, counting with a warp reduction. Same result as
+// down, two bits per step, counting with warp reductions. Same result as
 // warp_select_kth, without its shared-memory histogram passes.
 __device__ __forceinline__ uint32_t warp_select_kth_small(const uint32_t* keys, int n, int k) {
     constexpr int PER = FCAP / 32;
@@ -725,18 +725,46 @@ __device__ __forceinline__ uint32_t warp_select_kth_small(const uint32_t* keys, 
     uint32_t mask = ~((2u << hi) - 1u);  // bits above hi: the same in every key
     uint32_t prefix = a & mask;
     unsigned krem = (unsigned)k;
+    int b = hi;
+    // two bits per step: the counts of the digits 3, 2 and 1 among the keys
+    // that match the prefix (three independent reductions)
 #pragma unroll 1
-    for (int b = hi; b >= 0; --b) {
-        const uint32_t tm = mask | (1u << b), tc = prefix | (1u << b);
+    for (; b >= 1; b -= 2) {
+        const uint32_t tm = mask | (3u << (b - 1));
+        unsigned c3 = 0, c2 = 0, c1 = 0;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const bool in = lane + 32 * j < n && (kv[j] & mask) == prefix;
+            const uint32_t d = (kv[j] >> (b - 1)) & 3u;
+            c3 += (in && d == 3u) ? 1u : 0u;
+            c2 += (in && d == 2u) ? 1u : 0u;
+            c1 += (in && d == 1u) ? 1u : 0u;
+        }
+        c3 = __reduce_add_sync(0xffffffffu, c3);
+        c2 = __reduce_add_sync(0xffffffffu, c2);
+        c1 = __reduce_add_sync(0xffffffffu, c1);
+        uint32_t d;
+        if (c3 >= krem) {
+            d = 3u;
+        } else if (c3 + c2 >= krem) {
+            d = 2u;
+            krem -= c3;
+        } else if (c3 + c2 + c1 >= krem) {
+            d = 1u;
+            krem -= c3 + c2;
+        } else {
+            d = 0u;
+            krem -= c3 + c2 + c1;
+        }
+        prefix |= d << (b - 1);
+        mask = tm;
+    }
+    if (b == 0) {  // one bit left
         unsigned c = 0;
 #pragma unroll
-        for (int j = 0; j < PER; ++j) c += (lane + 32 * j < n && (kv[j] & tm) == tc) ? 1u : 0u;
+        for (int j = 0; j < PER; ++j) c += (lane + 32 * j < n && (kv[j] & (mask | 1u)) == (prefix | 1u)) ? 1u : 0u;
         c = __reduce_add_sync(0xffffffffu, c);
-        if (c >= krem)
-            prefix = tc;
-        else
-            krem -= c;
-        mask = tm;
+        if (c >= krem) prefix |= 1u;
     }
     return prefix;
 }
