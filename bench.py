@@ -34,9 +34,9 @@ METRIC = "sampled rows/s (V=151936 fp32, top_k 50)"
 UNIT = "rows/s"
 # ncu dram__bytes_read.sum + dram__bytes_write.sum of one stream_select_kernel
 # launch per row of this workload, from a 512-row capture of the same kernel
-# (profiles/stream_select_kernel_c5.md): 311,259,904 + 5,503,232 bytes / 512 rows.
+# (profiles/stream_select_kernel_c5.md): 311,272,960 + 4,212,480 bytes / 512 rows.
 # Traffic grows in proportion to the rows, so it is scaled to a full launch.
-NCU_TRAFFIC_BYTES_PER_ROW = (311259904 + 5503232) / 512
+NCU_TRAFFIC_BYTES_PER_ROW = (311272960 + 4212480) / 512
 DOMINANT_KERNEL = "mxs::stream_select_kernel"
 
 
