@@ -161,6 +161,72 @@ def run_reference_arm(args):
     return 0
 
 
+def run_vocab_mode(args):
+    """Vocab-sharded sampling (not the headline line): every rank holds the same
+    rows but only its column shard of the vocabulary, and one C-ABI call per
+    rank (mxs_sample_vocabsharded over an NCCL communicator) samples every row.
+    The job processes `rows` rows per step whatever the number of GPUs, so
+    scaling is strong; the value is rows per second of the whole job, timed on
+    the device, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    import mxs_sampler
+    from mxs_sampler import nccl
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    if V % world:
+        raise SystemExit(f"vocab {V} does not split over {world} ranks")
+    cols = V // world
+    rows = args.rows
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)  # the same rows on every rank
+    full = torch.randn((rows, V), generator=gen, device=dev, dtype=torch.float32) * SIGMA
+    u = torch.rand(rows, generator=gen, device=dev, dtype=torch.float64)
+    shard = full[:, rank * cols:(rank + 1) * cols].contiguous()
+    del full
+    obj = [nccl.get_unique_id() if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(obj, 0)
+    comm = nccl.comm_init_rank(world, obj[0], rank)
+
+    def step():
+        mxs_sampler.sample_vocabsharded(shard, TEMPERATURE, TOP_K, u, comm)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item()) / args.steps
+    nccl.comm_destroy(comm)
+    if rank == 0:
+        print(json.dumps({
+            "mode": "vocab-sharded", "metric": METRIC, "value": rows / (ms_step / 1e3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "dtype": "f32",
+            "data": "synthetic (torch.randn seeded, N(0,2^2))",
+            "config": {"workload": f"c5 vocab-sharded: [{rows} x {V}] fp32, {world} x {cols} columns, T=0.8, "
+                                   "top_k 50", "parallelism": f"vocab-sharded x{world}, NCCL all-gather of "
+                                   "candidate lists", "l2": "inputs larger than L2; no flush"}}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -171,8 +237,12 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--mode", default="row", choices=["row", "vocab"],
+                    help="row: the headline (row-sharded, weak scaling); vocab: vocab-sharded over NCCL")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.mode == "vocab" and args.impl != "reference":
+        return run_vocab_mode(args)
     if args.impl == "reference":
         return run_reference_arm(args)
 
