@@ -402,7 +402,9 @@ int mxs_shard_candidates(const float* d_shard_logits, int64_t rows, int64_t shar
     Device* d;
     int rc = current_device(&d);
     if (rc) return rc;
-    const Plan pl = make_plan(*d, rows, shard_cols, k_use, false);
+    // k <= KSPLIT on 16-byte aligned rows: the two-kernel path, whose finish
+    // kernel writes the lists (MODE_EMIT); otherwise the CTA kernels.
+    const Plan pl = make_plan(*d, rows, shard_cols, k_use, false, use_split(shard_cols, ld, d_shard_logits, k_use));
     rc = ensure_library_ws(*d, pl.total, (cudaStream_t)stream);
     if (rc) return rc;
     Params p{};

@@ -780,6 +780,87 @@ __device__ unsigned long long g_fin_prof[8];
 #define MXS_FIN_ADD(i, x) (void)0
 #endif
 
+// Gather row `row`'s candidate list into w.keys / w.idx: taken in batches
+// against a running bound (the k-th largest key held once the buffer has
+// filled), so lists longer than the buffer (a row split over many chunks)
+// still fit. Returns the count; sets *massive when ties keep the buffer full.
+__device__ __forceinline__ int gather_row_list(const Params& p, int64_t row, FinishWarpSmem& w, uint32_t cnt_all,
+                                           int k, bool* massive) {
+    const int lane = threadIdx.x & 31;
+    bool exact = false;
+    const uint64_t* src = p.row_cand + row * (int64_t)p.row_cap;
+    const uint32_t lt = (1u << lane) - 1u;
+    int cnt = 0;
+    uint32_t bound = 0u;
+    // 256 entries per load round trip (8 per lane in flight).
+    for (int i0 = 0; i0 < (int)cnt_all && !exact; i0 += 256) {
+        uint64_t vv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = i0 + 32 * j + lane;
+            vv[j] = i < (int)cnt_all ? src[i] : 0ull;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (exact || i0 + 32 * j >= (int)cnt_all) break;
+            const int i = i0 + 32 * j + lane;
+            const uint64_t v = vv[j];
+            const bool take = i < (int)cnt_all && (uint32_t)(v >> 32) >= bound;
+            const uint32_t bal = __ballot_sync(0xffffffffu, take);
+            if (take) {
+                const int pos = cnt + __popc(bal & lt);
+                w.keys[pos] = (uint32_t)(v >> 32);
+                w.idx[pos] = (int32_t)(uint32_t)v;
+            }
+            cnt += __popc(bal);
+            __syncwarp();
+            if (cnt > FCAP - 32) {
+                MXS_FIN_ADD(7, 1);
+                bound = warp_select_kth_small(w.keys, cnt, k);
+                cnt = warp_compact_ge(w.keys, w.idx, cnt, bound);
+                if (cnt > FCAP - 32) exact = true;  // massive ties
+            }
+        }
+    }
+    *massive = exact;
+    return cnt;
+}
+
+// MODE_EMIT (vocab-sharded step 1 on this path): publish row `row`'s candidate
+// list - every logit of the shard >= the shard's k-th largest value - with
+// global column indices, as the CTA kernels' emit_list does. A row the list
+// cannot represent (NaN, overflow, massive ties) gets a count of 0 and a flag,
+// and the merge hands it back.
+__device__ void emit_row_warp(const Params& p, int64_t row, FinishWarpSmem& w) {
+    const int lane = threadIdx.x & 31;
+    const int k = p.k_use;
+    uint32_t flags = p.row_flag[row] & (FLAG_NAN | FLAG_OVERFLOW | FLAG_TIMEOUT);
+    const uint32_t cnt_all = p.row_cnt[row];
+    if (!flags && (cnt_all > (uint32_t)p.row_cap || cnt_all < (uint32_t)k)) flags |= FLAG_OVERFLOW;
+    int cnt = 0;
+    if (!flags) {
+        bool massive = false;
+        cnt = gather_row_list(p, row, w, cnt_all, k, &massive);
+        if (massive) flags |= FLAG_OVERFLOW;
+        if (!flags && cnt > k) {
+            const uint32_t kth = warp_select_kth_small(w.keys, cnt, k);
+            cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
+        }
+        if (cnt > p.out_cap) flags |= FLAG_OVERFLOW;
+        if (flags) cnt = 0;
+    }
+    uint64_t* dst = p.out_cand + row * p.out_cap;
+    for (int i = lane; i < cnt; i += 32)
+        dst[i] = ((uint64_t)w.keys[i] << 32) | (uint32_t)(w.idx[i] + (int32_t)p.col_offset);
+    if (lane == 0) {
+        p.out_count[row] = (uint32_t)cnt;
+        p.out_flags[row] = flags;
+        if (flags & FLAG_TIMEOUT) atomicOr(p.status, flags);
+        p.row_cnt[row] = 0u;  // left clear for the next call on this workspace
+        p.row_flag[row] = 0u;
+    }
+}
+
 __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w, uint32_t* out_flags) {
     const int lane = threadIdx.x & 31;
     MXS_FIN_T(f0);
@@ -789,43 +870,9 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
     bool exact = (flags & (FLAG_NAN | FLAG_OVERFLOW)) != 0 || cnt_all > (uint32_t)p.row_cap ||
                  cnt_all < (uint32_t)k;
     if (!(flags & FLAG_TIMEOUT) && !exact) {
-        // Take the list in batches of 32 against a running bound (the k-th
-        // largest key held once the buffer has filled), so lists longer than
-        // the buffer (a row split over many chunks) still fit.
-        const uint64_t* src = p.row_cand + row * (int64_t)p.row_cap;
-        const uint32_t lt = (1u << lane) - 1u;
-        int cnt = 0;
-        uint32_t bound = 0u;
-        // 256 entries per load round trip (8 per lane in flight).
-        for (int i0 = 0; i0 < (int)cnt_all && !exact; i0 += 256) {
-            uint64_t vv[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = i0 + 32 * j + lane;
-                vv[j] = i < (int)cnt_all ? src[i] : 0ull;
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                if (exact || i0 + 32 * j >= (int)cnt_all) break;
-                const int i = i0 + 32 * j + lane;
-                const uint64_t v = vv[j];
-                const bool take = i < (int)cnt_all && (uint32_t)(v >> 32) >= bound;
-                const uint32_t bal = __ballot_sync(0xffffffffu, take);
-                if (take) {
-                    const int pos = cnt + __popc(bal & lt);
-                    w.keys[pos] = (uint32_t)(v >> 32);
-                    w.idx[pos] = (int32_t)(uint32_t)v;
-                }
-                cnt += __popc(bal);
-                __syncwarp();
-                if (cnt > FCAP - 32) {
-                    MXS_FIN_ADD(7, 1);
-                    bound = warp_select_kth_small(w.keys, cnt, k);
-                    cnt = warp_compact_ge(w.keys, w.idx, cnt, bound);
-                    if (cnt > FCAP - 32) exact = true;  // massive ties
-                }
-            }
-        }
+        bool massive = false;
+        int cnt = gather_row_list(p, row, w, cnt_all, k, &massive);
+        exact = massive;
         // Ties among the survivors, or across the cut, make the reference's
         // order of the equal values a product of its heap process. The
         // probabilities and their running sums depend only on the values by
@@ -878,6 +925,15 @@ static_assert(F_WARPS * 32 == NT, "the replay needs a CTA of NT threads");
 
 // Three CTAs per SM (80 registers): the per-warp replays are latency-bound, so
 // more resident warps replay more rows at once.
+// Batches of at most this many rows (148 SMs x 3 resident CTAs) get one CTA
+// per row: the GPU has room for them, and a tie row then always has a whole
+// CTA to replay it, which is faster for a lone row than a warp.
+constexpr int64_t FINISH_ONE_ROW_PER_CTA = 444;
+
+__device__ __forceinline__ int finish_rows_per_cta(int64_t rows) {
+    return rows <= FINISH_ONE_ROW_PER_CTA ? 1 : F_WARPS;
+}
+
 __global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) {
     extern __shared__ __align__(128) unsigned char fsmem[];
     __shared__ Ent s_heap[HEAP_SMEM_MAX];
@@ -886,7 +942,8 @@ __global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) 
     __shared__ int s_xn, s_wn;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     FinishWarpSmem& w = reinterpret_cast<FinishWarpSmem*>(fsmem)[warp];
-    const int64_t row = (int64_t)blockIdx.x * F_WARPS + warp;
+    const int rpc = finish_rows_per_cta(p.rows);
+    const int64_t row = warp < rpc ? (int64_t)blockIdx.x * rpc + warp : p.rows;  // p.rows: no row
     if (threadIdx.x == 0) s_xn = s_wn = 0;
     MXS_PROF_BEGIN();
     csync();
@@ -935,6 +992,15 @@ extern "C" __attribute__((visibility("default"))) int mxs_prof_read_finish(unsig
 }
 #endif
 
+// MODE_EMIT's second kernel: one warp per row writes the shard's candidate
+// list (its own kernel: the branch inside finish_rows_kernel slowed sampling).
+__global__ void __launch_bounds__(F_WARPS * 32) emit_rows_kernel(Params p) {
+    __shared__ FinishWarpSmem ws[F_WARPS];
+    const int warp = threadIdx.x >> 5;
+    const int64_t row = (int64_t)blockIdx.x * F_WARPS + warp;
+    if (row < p.rows) emit_row_warp(p, row, ws[warp]);
+}
+
 size_t stream_smem_bytes() { return S_SMEM; }
 
 cudaError_t stream_path_configure(int* blocks_per_sm) {
@@ -952,7 +1018,12 @@ cudaError_t stream_path_launch(const Params& p, int grid, cudaStream_t stream, c
     cudaError_t e = cudaGetLastError();
     if (ev_stop) cudaEventRecord(ev_stop, stream);
     if (e != cudaSuccess) return e;
-    finish_rows_kernel<<<(unsigned)((p.rows + F_WARPS - 1) / F_WARPS), F_WARPS * 32, F_SMEM, stream>>>(p);
+    if (p.mode == MODE_EMIT) {
+        emit_rows_kernel<<<(unsigned)((p.rows + F_WARPS - 1) / F_WARPS), F_WARPS * 32, 0, stream>>>(p);
+        return cudaGetLastError();
+    }
+    const int64_t rpc = p.rows <= FINISH_ONE_ROW_PER_CTA ? 1 : F_WARPS;
+    finish_rows_kernel<<<(unsigned)((p.rows + rpc - 1) / rpc), F_WARPS * 32, F_SMEM, stream>>>(p);
     return cudaGetLastError();
 }
 
