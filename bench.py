@@ -33,9 +33,9 @@ SIGMA = 2.0
 METRIC = "sampled rows/s (V=151936 fp32, top_k 50)"
 UNIT = "rows/s"
 # ncu dram__bytes_read.sum + dram__bytes_write.sum of one stream_select_kernel
-# launch per row of this workload, from a 512-row capture of the same kernel
-# (profiles/stream_select_kernel_c5.md): 311,272,960 + 4,212,480 bytes / 512 rows.
-# Traffic grows in proportion to the rows, so it is scaled to a full launch.
+# launch per row of this workload, from an ncu capture of a 512-row launch of the
+# same kernel: 311,272,960 + 4,212,480 bytes / 512 rows. Traffic grows in
+# proportion to the rows, so it is scaled to a full launch.
 NCU_TRAFFIC_BYTES_PER_ROW = (311272960 + 4212480) / 512
 DOMINANT_KERNEL = "mxs::stream_select_kernel"
 
@@ -79,6 +79,13 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_first(self, timeout=10.0):
+        """Block until the sampler has printed its first line, so that its
+        start-up (a heavy process launch) ends before the timed region."""
+        t_end = time.time() + timeout
+        while self.proc and not self.lines and time.time() < t_end:
+            time.sleep(0.02)
+
     def __exit__(self, *a):
         if self.proc:
             self.proc.terminate()
@@ -103,10 +110,20 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 def cpu_reference_run(rows_sample, seconds, threads=0):
     """Time the reference's sampling block (or the oracle port) on host cores.
     Returns (rows/s, kind, cores, description)."""
-    import numpy as np
     import oracle_lib
     import workloads
     if not os.path.exists(oracle_lib.ORACLE_SO):
@@ -133,7 +150,7 @@ def cpu_reference_run(rows_sample, seconds, threads=0):
     what = ("the reference's own sampling block (src/api/minxfmr.cpp:2091-2171, oracle/_ref)"
             if kind == "reference" else "the oracle port of that block")
     desc = (f"{what} on {done} rows ({rows_sample}-row batches of the same N(0,2^2) x 151936 workload, "
-            f"T=0.8, top_k 50) over {el:.1f} s, {cores} threads")
+            f"T=0.8, top_k 50) over {el:.1f} s, {cores} thread{'s' if cores > 1 else ''}")
     return done / el, kind, cores, desc
 
 
@@ -155,76 +172,114 @@ def run_reference_arm(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
             "config": {"workload": f"c5 throughput: {rows_sample}-row sample per step of [4096 x {V}] fp32 "
                                    f"N(0,2^2), T=0.8, top_k 50 (host cores)"},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc,
+                             "cpu_model": cpu_model()},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
-def run_vocab_mode(args):
-    """Vocab-sharded sampling (not the headline line): every rank holds the same
-    rows but only its column shard of the vocabulary, and one C-ABI call per
-    rank (mxs_sample_vocabsharded over an NCCL communicator) samples every row.
-    The job processes `rows` rows per step whatever the number of GPUs, so
-    scaling is strong; the value is rows per second of the whole job, timed on
-    the device, max over ranks."""
+def _gather_floats(vals, dev, world):
+    """Every rank's list of floats, on every rank (row r = rank r)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    if world == 1:
+        return [vals]
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.tolist() for o in out]
+
+
+def vocab_measure(rows, steps, warmup, check_rows=64):
+    """Vocab-sharded sampling of `rows` rows of the c5 workload: every rank holds
+    the same rows but only its column shard (V / world columns), and one C-ABI
+    call per rank (mxs_sample_vocabsharded over an NCCL communicator) samples
+    every row. Strong scaling: the job processes `rows` rows per step whatever
+    the number of GPUs. Timed on the device, max over ranks. Parity: rank 0
+    compares next, top-k order and probabilities of the first `check_rows`
+    rows with the CPU oracle on the full rows. Returns the record on rank 0."""
+    import numpy as np
     import torch
     import torch.distributed as dist
     import mxs_sampler
     from mxs_sampler import nccl
 
     rank, world, local = env_rank()
-    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
     if V % world:
         raise SystemExit(f"vocab {V} does not split over {world} ranks")
     cols = V // world
-    rows = args.rows
     gen = torch.Generator(device=dev)
-    gen.manual_seed(1234)  # the same rows on every rank
+    gen.manual_seed(4321)  # the same rows on every rank
     full = torch.randn((rows, V), generator=gen, device=dev, dtype=torch.float32) * SIGMA
     u = torch.rand(rows, generator=gen, device=dev, dtype=torch.float64)
     shard = full[:, rank * cols:(rank + 1) * cols].contiguous()
+    check = full[:check_rows].cpu().numpy() if rank == 0 else None
     del full
     obj = [nccl.get_unique_id() if rank == 0 else None]
     if world > 1:
         dist.broadcast_object_list(obj, 0)
     comm = nccl.comm_init_rank(world, obj[0], rank)
+    stream = torch.cuda.current_stream()
 
-    def step():
-        mxs_sampler.sample_vocabsharded(shard, TEMPERATURE, TOP_K, u, comm)
+    def step(topk=False):
+        return mxs_sampler.sample_vocabsharded(shard, TEMPERATURE, TOP_K, u, comm, stream=stream)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(args.steps):
+    ev0.record(stream)
+    for _ in range(steps):
         step()
-    ev1.record()
+    ev1.record(stream)
     torch.cuda.synchronize()
-    t = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    ms = ev0.elapsed_time(ev1)
+    per_rank = _gather_floats([ms / steps], dev, world)
+    ms_step = max(r[0] for r in per_rank)
+    nxt, idx, prob, flg = step()
+    torch.cuda.synchronize()
+    nccl.comm_destroy(comm)
     if world > 1:
         dist.barrier()
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_step = float(t.item()) / args.steps
-    nccl.comm_destroy(comm)
+    if rank != 0:
+        return None
+    import oracle_lib
+    uc = u[:check_rows].cpu().numpy()
+    n0, i0, p0 = oracle_lib.oracle_sample(check, TEMPERATURE, TOP_K, uc, threads=os.cpu_count() or 1)
+    g_n, g_i, g_p = nxt[:check_rows].cpu().numpy(), idx[:check_rows].cpu().numpy(), prob[:check_rows].cpu().numpy()
+    bad = (g_n != n0) | (g_i != i0).any(axis=1) | (np.abs(g_p - p0) > 1e-6 * np.abs(p0)).any(axis=1)
+    exact_rows = int(((flg.cpu().numpy() & mxs_sampler.ROW_EXACT) != 0).sum())
+    return {"value": rows / (ms_step / 1e3), "unit": UNIT, "ms_per_step": ms_step, "steps": steps,
+            "scaling": "strong", "rows": rows, "shards": world, "shard_cols": cols,
+            "per_rank_ms_per_step": [r[0] for r in per_rank],
+            "parity_rows_checked": check_rows, "parity_mismatch_rows": int(bad.sum()),
+            "full_row_pass_rows": exact_rows,
+            "workload": f"[{rows} x {V}] fp32 N(0,2^2), T=0.8, top_k 50, {world} x {cols} columns, "
+                        "one mxs_sample_vocabsharded call per rank (NCCL all-gather of candidate lists)"}
+
+
+def run_vocab_mode(args):
+    """--mode vocab: the vocab-sharded measurement alone (not the headline line)."""
+    import torch
+    import torch.distributed as dist
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    rec = vocab_measure(args.rows, args.steps, max(args.warmup, 3))
     if rank == 0:
-        print(json.dumps({
-            "mode": "vocab-sharded", "metric": METRIC, "value": rows / (ms_step / 1e3), "unit": UNIT,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "strong", "dtype": "f32",
-            "data": "synthetic (torch.randn seeded, N(0,2^2))",
-            "config": {"workload": f"c5 vocab-sharded: [{rows} x {V}] fp32, {world} x {cols} columns, T=0.8, "
-                                   "top_k 50", "parallelism": f"vocab-sharded x{world}, NCCL all-gather of "
-                                   "candidate lists", "l2": "inputs larger than L2; no flush"}}), flush=True)
+        line = {"mode": "vocab-sharded", "metric": METRIC, "n_gpus": world, "warmup": args.warmup,
+                "higher_is_better": True, "dtype": "f32", "data": "synthetic (torch.randn seeded, N(0,2^2))"}
+        line.update(rec)
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+    return 0
 
 
 def main():
@@ -237,6 +292,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-vocab", action="store_true", help="skip the vocab-sharded sub-record (N > 1)")
     ap.add_argument("--mode", default="row", choices=["row", "vocab"],
                     help="row: the headline (row-sharded, weak scaling); vocab: vocab-sharded over NCCL")
     args = ap.parse_args()
@@ -251,10 +307,10 @@ def main():
     import mxs_sampler
 
     rank, world, local = env_rank()
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
     rows = args.rows
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
@@ -277,7 +333,9 @@ def main():
     for a, b in kev:  # torch creates the CUDA events on their first record
         a.record(stream)
         b.record(stream)
+    torch.cuda.synchronize()
     with ClockSampler(gpu_index) as clk:
+        clk.wait_first()  # the sampler's start-up stays out of the timed region
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -300,17 +358,14 @@ def main():
             for _ in range(50):
                 step()
             torch.cuda.synchronize()
-    t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    per_rank = _gather_floats([ms_total / args.steps, kernel_ms], dev, world)
+    ms_max = max(r[0] for r in per_rank) * args.steps
     ms_step = ms_max / args.steps
     value = world * rows * args.steps / (ms_max / 1e3)
 
     # end to end through the host-buffer C-ABI entry: pinned logits in, ids out
     e2e = None
     if not args.no_e2e:
-        import numpy as np
         h_logits = torch.empty((rows, V), dtype=torch.float32).pin_memory()
         h_logits.copy_(logits.cpu())
         h_u = u.cpu().pin_memory()
@@ -327,6 +382,13 @@ def main():
         e2e = {"value": world * rows * n_e2e / float(el.item()), "unit": UNIT,
                "h2d_bytes_per_step": rows * V * 4 + rows * 8, "d2h_bytes_per_step": rows * 4,
                "steps": n_e2e, "timing": "host wall clock around synchronous calls (max over ranks)"}
+        del h_logits
+
+    vocab = None
+    if world > 1 and not args.no_vocab:
+        del logits
+        torch.cuda.empty_cache()
+        vocab = vocab_measure(rows, max(3, min(args.steps, 50)), args.warmup)
 
     if rank == 0:
         peak, peak_kind = peaks()
@@ -342,7 +404,11 @@ def main():
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             v, kind, cores, desc = cpu_reference_run(256, args.cpu_seconds)
-            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc}
+            v1, _, _, desc1 = cpu_reference_run(16, min(5.0, args.cpu_seconds), threads=1)
+            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc,
+                   "cpu_model": cpu_model(),
+                   "single_thread": {"value": v1, "unit": UNIT, "cores": 1, "sample": desc1,
+                                     "note": "one row at a time, as the reference samples"}}
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (torch.randn seeded, N(0,2^2))",
@@ -351,7 +417,11 @@ def main():
                            "temperature": TEMPERATURE, "parallelism": f"row-sharded x{world}, no collective",
                            "l2": "inputs (2.49 GB per GPU) larger than L2; no flush"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps,
-                "hbm_frac_of_8tbs": achieved / 8000.0, "clocks": clk.summary()}
+                "hbm_frac_of_8tbs": achieved / 8000.0, "clocks": clk.summary(),
+                "per_rank": [{"rank": r, "ms_per_step": v[0], "stream_kernel_ms": v[1]}
+                             for r, v in enumerate(per_rank)]}
+        if vocab is not None:
+            line["vocab_sharded"] = vocab
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -185,23 +185,41 @@ MXS_API int mxs_set_profile_events(void* start, void* stop);
  * cannot allocate device memory (hosts whose memory pool owns the whole GPU, or
  * that forbid allocation on the per-token path). Same arguments and results as
  * mxs_sample_topk_ex without a workspace: the scratch is a fixed array of
- * MXS_NOALLOC_SCRATCH_BYTES compiled into the library, held by every GPU that
- * loads it until the process exits; no call allocates or frees memory.
+ * MXS_NOALLOC_SCRATCH_BYTES (48 MiB) compiled into the library, held by every
+ * GPU that loads it until the process exits; no call allocates or frees memory.
  * Returns MXS_ERR_WORKSPACE when the shape needs more scratch than that
- * (mxs_workspace_size tells how much; large top_k, above ~3000, needs the most).
+ * (mxs_workspace_size tells how much). On the default path (top_k <= 128,
+ * 16-byte aligned rows) the need is about rows x 8 KiB at any vocabulary, so
+ * up to about 6,000 rows fit (the 4096-row batch of the throughput benchmark
+ * does); top_k above 2048 needs the most (two k-entry slots per CTA).
+ * Timeouts of these calls reach mxs_get_status like any other call's.
  * The first call on a device looks up the array's device address; make that
  * call before any stream capture. All calls share the one array, so calls
  * that overlap on the GPU (other streams, other threads) race and must be
  * serialised by the caller.
  */
-#define MXS_NOALLOC_SCRATCH_BYTES (16u << 20)
+#define MXS_NOALLOC_SCRATCH_BYTES (48u << 20)
 MXS_API int mxs_sample_topk_noalloc(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld,
                                     double temperature, int top_k, double top_p, double min_p, const double* d_u,
                                     int32_t* d_next, int32_t* d_topk_idx, double* d_topk_prob,
                                     uint32_t* d_row_flags, void* stream);
 
+/*
+ * Test hooks of this library's own tests (no counterpart in the reference).
+ * Nothing else changes them: a sampling call never reads the environment.
+ *   drop_tile        CTA 0's streaming producer stops before its tile with this
+ *                    sequence number, so its consumers' bounded wait runs out and
+ *                    the rows report MXS_ROW_TIMEOUT (-1: off, the default)
+ *   replay_warp_min  a finish CTA replays its tie rows one per warp when it holds
+ *                    at least this many, else with the whole CTA (default 2)
+ *   path             0: default planning; 2: the CTA-synchronous kernel for every k
+ * Process-wide; calls already enqueued keep the hooks they were launched with.
+ */
+MXS_API int mxs_set_test_hooks(int64_t drop_tile, int replay_warp_min, int path);
+
 /* OR of MXS_ROW_* flags of every row that hit MXS_ROW_TIMEOUT since the last clear
- * on the current device (synchronises the device). */
+ * on the current device, from every entry point and workspace (a sticky word per
+ * device that every launch ORs into; synchronises the device). */
 MXS_API int mxs_get_status(uint32_t* flags, int clear);
 
 /* Library version string. */

@@ -29,8 +29,14 @@ struct HostBuffers {
     size_t rows_cap = 0, topk_cap = 0;
 };
 
+// Sticky status word of each device: every sampling launch ORs the flags of its
+// timed-out rows into it, whichever workspace the call used (library-owned,
+// caller-owned or the fixed array of the allocation-free entry point).
+__device__ uint32_t g_status_word;
+
 struct Device {
     bool ready = false;
+    uint32_t* status = nullptr;  // device address of g_status_word on this device
     int sms = 0;
     int blocks_per_sm = 0;
     void* ws = nullptr;  // library-owned workspace (zeroed at allocation)
@@ -59,6 +65,9 @@ int current_device(Device** out) {
         int bps2 = 0;
         if (mxs::stream_path_configure(&bps2) != cudaSuccess || bps2 < 1) return MXS_ERR_CUDA;
         bps = std::min(bps, bps2);
+        void* st = nullptr;
+        if (cudaGetSymbolAddress(&st, g_status_word) != cudaSuccess || !st) return MXS_ERR_CUDA;
+        d.status = static_cast<uint32_t*>(st);
         d.sms = prop.multiProcessorCount;
         d.blocks_per_sm = bps;
         d.ready = true;
@@ -86,19 +95,19 @@ int clamp_k(int top_k, int64_t vocab) {
     return (int)k;
 }
 
+// Test hooks (mxs_set_test_hooks; off unless a test sets them). Plain values,
+// never read from the environment, so nothing outside the caller's own calls
+// can change what a sampling call does.
+struct TestHooks {
+    int64_t drop_tile = -1;     // CTA 0's streaming producer stops before this tile (-1: off)
+    int replay_warp_min = 2;    // tie rows of a finish CTA replayed one per warp from this many
+    int path = 0;               // 0: default planning; 2: the CTA-synchronous kernel for every k
+};
+TestHooks g_hooks;
+
 // The two-kernel path takes sampling calls with k <= KSPLIT on 16-byte aligned
-// rows. MXS_SAMPLER_PATH selects another kernel for every call ("fused": the
-// one-launch warp-specialised kernel, "block": the CTA-synchronous one); the
-// parity tests run all three. MXS_SAMPLER_BLOCK_PATH=1 is the older spelling of
-// "block".
-int path_override() {
-    const char* bp = getenv("MXS_SAMPLER_BLOCK_PATH");
-    if (bp && bp[0] == '1') return 2;
-    const char* ps = getenv("MXS_SAMPLER_PATH");
-    if (ps && ps[0] == 'f') return 1;
-    if (ps && ps[0] == 'b') return 2;
-    return 0;
-}
+// rows, unless a test forced the CTA-synchronous kernel.
+int path_override() { return g_hooks.path; }
 
 // Candidate list entries per row: a row split over S chunks gets up to 256 per
 // chunk (each chunk keeps at least k of its own logits).
@@ -192,9 +201,9 @@ int ensure_library_ws(Device& d, size_t bytes, cudaStream_t stream) {
     return MXS_OK;
 }
 
-void fill_workspace(Params& p, const Plan& pl, void* ws) {
+void fill_workspace(Params& p, const Plan& pl, void* ws, const Device& d) {
     char* b = static_cast<char*>(ws);
-    p.status = reinterpret_cast<uint32_t*>(b + pl.off_status);
+    p.status = d.status;
     p.row_counter = reinterpret_cast<uint32_t*>(b + pl.off_counter);
     p.row_state = reinterpret_cast<uint32_t*>(b + pl.off_state);
     p.chunk_count = reinterpret_cast<uint32_t*>(b + pl.off_ccount);
@@ -222,15 +231,8 @@ int launch(Params& p, const Plan& pl, cudaStream_t stream, int sms = 148, cudaEv
     p.units = pl.units;
     p.outcap = pl.outcap;
     if (pl.split) {
-        // MXS_DEBUG_DROP_TILE=n (tests only): CTA 0's producer stops before its
-        // n-th tile, so its consumers' bounded wait runs out (MXS_ROW_TIMEOUT).
-        const char* dt = getenv("MXS_DEBUG_DROP_TILE");
-        p.debug_drop_tile = dt ? atoll(dt) : -1;
-        // MXS_REPLAY_WARP_MIN=n (tests): replay a finish CTA's tie rows one per
-        // warp when it holds n or more of them (default 2; 1 = always per warp,
-        // 9 = always with the whole CTA).
-        const char* rw = getenv("MXS_REPLAY_WARP_MIN");
-        p.replay_warp_min = rw ? atoi(rw) : 2;
+        p.debug_drop_tile = g_hooks.drop_tile;
+        p.replay_warp_min = g_hooks.replay_warp_min;
         const bool clean = lib_ws_owner && lib_ws_owner->clean_rows == p.rows && lib_ws_owner->clean_off == pl.off_rcnt;
         if (lib_ws_owner) lib_ws_owner->clean_rows = -1;
         if (!clean && cudaMemsetAsync(p.row_cnt, 0, pl.zero_bytes, stream) != cudaSuccess) return MXS_ERR_CUDA;
@@ -243,9 +245,6 @@ int launch(Params& p, const Plan& pl, cudaStream_t stream, int sms = 148, cudaEv
     }
     if (lib_ws_owner) lib_ws_owner->clean_rows = -1;
     const bool tma = (reinterpret_cast<uintptr_t>(p.logits) % 16 == 0) && (p.ld % 4 == 0);
-    // MXS_SAMPLER_BLOCK_PATH=1 selects the CTA-synchronous streaming kernel for
-    // every k (the parity tests run both kernels).
-    p.force_block_path = path_override() == 2 ? 1 : 0;
     if (ev0) cudaEventRecord(ev0, stream);
     if (mxs::sample_kernel_launch(p, pl.grid, tma, stream) != cudaSuccess) return MXS_ERR_CUDA;
     if (ev1) cudaEventRecord(ev1, stream);
@@ -257,6 +256,22 @@ bool ws_ok(const void* ws, size_t bytes, size_t need) {
 }
 
 }  // namespace
+
+namespace mxs {
+// Bytes at the start of every workspace layout on the current device that must
+// read zero when a call starts: the CTA-synchronous kernel's per-row chunk
+// counters, which sit at offsets that depend on the device alone. (The
+// two-kernel path's per-row counters are cleared by every call on a caller
+// workspace before its launch.)
+int workspace_zero_prefix(size_t* bytes) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Device* d;
+    int rc = current_device(&d);
+    if (rc) return rc;
+    *bytes = make_plan(*d, 1, 1, 1, false).off_ccount;
+    return MXS_OK;
+}
+}  // namespace mxs
 
 extern "C" {
 
@@ -318,7 +333,7 @@ int mxs_sample_topk_ex(const float* d_logits, int64_t rows, int64_t vocab, int64
     p.topk_prob = d_topk_prob;
     p.row_flags = d_row_flags;
     p.mode = mxs::MODE_SAMPLE;
-    fill_workspace(p, pl, ws);
+    fill_workspace(p, pl, ws, *d);
     return launch(p, pl, (cudaStream_t)stream, d->sms, d->ev_start, d->ev_stop, d_workspace ? nullptr : d);
 }
 
@@ -420,7 +435,7 @@ int mxs_shard_candidates(const float* d_shard_logits, int64_t rows, int64_t shar
     p.out_flags = d_flags;
     p.out_cap = cap;
     d->clean_rows = -1;
-    fill_workspace(p, pl, d->ws);
+    fill_workspace(p, pl, d->ws, *d);
     return launch(p, pl, (cudaStream_t)stream);
 }
 
@@ -461,7 +476,7 @@ int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count_all, co
     p.nshards = nshards;
     p.in_cap = cap;
     d->clean_rows = -1;
-    fill_workspace(p, pl, d->ws);
+    fill_workspace(p, pl, d->ws, *d);
     p.logits = nullptr;
     // no logits: launch the plain variant (no bulk copies are issued in merge mode)
     p.S = pl.S;
@@ -483,18 +498,24 @@ int mxs_set_profile_events(void* start, void* stop) {
     return MXS_OK;
 }
 
+int mxs_set_test_hooks(int64_t drop_tile, int replay_warp_min, int path) {
+    if (replay_warp_min < 1 || (path != 0 && path != 2)) return MXS_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_hooks.drop_tile = drop_tile;
+    g_hooks.replay_warp_min = replay_warp_min;
+    g_hooks.path = path;
+    return MXS_OK;
+}
+
 int mxs_get_status(uint32_t* flags, int clear) {
     if (!flags) return MXS_ERR_INVALID;
     std::lock_guard<std::mutex> lk(g_mu);
     Device* d;
     int rc = current_device(&d);
     if (rc) return rc;
-    *flags = 0;
-    if (!d->ws) return MXS_OK;
     if (cudaDeviceSynchronize() != cudaSuccess) return MXS_ERR_CUDA;
-    // status sits at offset 0 of every workspace layout
-    if (cudaMemcpy(flags, d->ws, sizeof(uint32_t), cudaMemcpyDeviceToHost) != cudaSuccess) return MXS_ERR_CUDA;
-    if (clear && cudaMemset(d->ws, 0, sizeof(uint32_t)) != cudaSuccess) return MXS_ERR_CUDA;
+    if (cudaMemcpy(flags, d->status, sizeof(uint32_t), cudaMemcpyDeviceToHost) != cudaSuccess) return MXS_ERR_CUDA;
+    if (clear && cudaMemset(d->status, 0, sizeof(uint32_t)) != cudaSuccess) return MXS_ERR_CUDA;
     return MXS_OK;
 }
 

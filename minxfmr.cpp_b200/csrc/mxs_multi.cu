@@ -87,7 +87,10 @@ enum {
 };
 
 constexpr int MAX_DEVICES = 64;
-std::mutex g_mu;
+// One lock per device: ranks driven from threads of one process (one thread per
+// GPU, each with its own communicator) never block each other, since each
+// holds only its own device's lock across its collectives.
+std::mutex g_mu[MAX_DEVICES];
 Buf g_buf[MAX_DEVICES][NBUF];
 uint32_t* g_count_host[MAX_DEVICES];  // pinned: the number of rows needing the full-row pass
 
@@ -213,9 +216,9 @@ int mxs_sample_vocabsharded(const float* d_shard_logits, int64_t rows, int64_t s
     const int cap = 2 * (int)std::min<int64_t>(k_use, shard_cols) + 64;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-    std::lock_guard<std::mutex> lk(g_mu);
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return MXS_ERR_NO_DEVICE;
+    std::lock_guard<std::mutex> lk(g_mu[dev]);
     Buf* b = g_buf[dev];
     int rc;
     if ((rc = b[B_CAND].get(sizeof(uint64_t) * rows * cap)) || (rc = b[B_CNT].get(4 * rows)) ||

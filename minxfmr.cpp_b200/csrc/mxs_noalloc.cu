@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/mxs_sampler.h"
+#include "mxs_launch.h"
 
 namespace {
 
@@ -53,10 +54,15 @@ extern "C" int mxs_sample_topk_noalloc(const float* d_logits, int64_t rows, int6
     void* scratch = nullptr;
     rc = scratch_address(dev, &scratch);
     if (rc) return rc;
-    // The array keeps whatever the last call left; the counters the kernel
-    // relies on must read zero, so the part this call uses is cleared first
-    // (an asynchronous memset on the same stream allocates nothing).
-    if (cudaMemsetAsync(scratch, 0, need, (cudaStream_t)stream) != cudaSuccess) return MXS_ERR_CUDA;
+    // The array keeps whatever the last call left. The counters that must read
+    // zero at the start of a call are cleared on the call's stream (a memset
+    // allocates nothing): the device-fixed prefix here, the per-row counters of
+    // the two-kernel path inside mxs_sample_topk_ex. Everything else in the
+    // array is written before it is read.
+    size_t zero = 0;
+    rc = mxs::workspace_zero_prefix(&zero);
+    if (rc) return rc;
+    if (cudaMemsetAsync(scratch, 0, zero, (cudaStream_t)stream) != cudaSuccess) return MXS_ERR_CUDA;
     return mxs_sample_topk_ex(d_logits, rows, vocab, ld, temperature, top_k, top_p, min_p, d_u, d_next, d_topk_idx,
                               d_topk_prob, d_row_flags, scratch, (size_t)MXS_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -303,13 +303,14 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
         fence_mbar_init();
         pol = policy_evict_normal();
     }
+    if (tid == 0) sm.dead = 0u;
     csync();
     auto unit_tiles = [&](int64_t u) -> int {
         const int64_t t0 = (int64_t)(u % S) * TPC;
         return (int)min((int64_t)TPC, NTL - t0);
     };
     auto issue = [&]() {
-        if (pj >= nj) return;
+        if (pj >= nj || *reinterpret_cast<volatile uint32_t*>(&sm.dead)) return;
         const int64_t u = blockIdx.x + pj * G;
         const int64_t row = u / S;
         const int64_t a = ((int64_t)(u % S) * TPC + pt) * TILE;
@@ -399,7 +400,14 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
             const int s = cseq % STAGES;
             MXS_PROF_T0(tw);
             if (TMA) {
-                if (!mbar_wait_bounded(&sm.bar[s], (cseq / STAGES) & 1)) atomicOr(&sm.flags, FLAG_TIMEOUT);
+                // Once a wait has run out, no further copies are issued: the
+                // remaining tiles are not waited for and their rows are flagged.
+                if (*reinterpret_cast<volatile uint32_t*>(&sm.dead)) {
+                    atomicOr(&sm.flags, FLAG_TIMEOUT);
+                } else if (!mbar_wait_bounded(&sm.bar[s], (cseq / STAGES) & 1)) {
+                    atomicOr(&sm.flags, FLAG_TIMEOUT);
+                    *reinterpret_cast<volatile uint32_t*>(&sm.dead) = 1u;
+                }
             }
             MXS_PROF_ADD(0, tw);
             MXS_PROF_T0(tc);
@@ -476,8 +484,14 @@ __global__ void __launch_bounds__(NT, 2) sample_kernel(Params p) {
     }
     MXS_PROF_ADD(7, ttot);
     MXS_PROF_FLUSH();
-    if (TMA && tid == 0)
+    if (TMA && tid == 0) {
+        // Every issued copy must land before the CTA retires. After a timeout
+        // the waits above stopped; only the last STAGES copies can be in
+        // flight (a stage is reissued only after all threads waited for it).
+        for (uint32_t q = pseq > STAGES ? pseq - STAGES : 0; q < pseq; ++q)
+            (void)mbar_wait_bounded(&sm.bar[q % STAGES], (q / STAGES) & 1);
         for (int s = 0; s < STAGES; ++s) mbar_inval(&sm.bar[s]);
+    }
 }
 
 #ifdef MXS_PROFILE
@@ -493,285 +507,6 @@ extern "C" __attribute__((visibility("default"))) int mxs_prof_read(unsigned lon
 
 
 // ---------------------------------------------------------------------------
-// Warp-specialised streaming kernel (aligned rows, k <= KWS): warp 8 is the
-// producer, issuing one bulk copy per TILE into a STAGES ring (stage full /
-// stage empty mbarriers); warps 0-7 each filter a 512-logit slice of every tile
-// into a private candidate buffer, without any CTA-wide barrier while a unit
-// streams. A warp whose buffer passes WTRIG selects its own k-th largest key
-// (k entries of the unit are >= it, so it is a valid lower bound for the whole
-// unit), compacts, and publishes it with atomicMax; every warp filters against
-// the highest bound published.
-// ---------------------------------------------------------------------------
-
-// Tighten the shared bound and compact the warp's buffer to it. The warp
-// publishes the m-th largest key it holds (m = ceil(k / NWARPS)); the consumer
-// warps filter disjoint slices of the unit, so at least NWARPS * m >= k logits
-// are >= the smallest value published by all of them, which is therefore a
-// valid bound, close to the unit's k-th largest. Until every warp has published,
-// a warp holding k or more entries offers its own k-th largest instead.
-__device__ __forceinline__ void warp_shrink(uint32_t* wk, int32_t* wi, int& wcnt, int k, uint32_t* hist, Misc& sm) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int m = (k + NWARPS - 1) / NWARPS;
-    if (wcnt >= m) {
-        const uint32_t km = warp_select_kth(wk, wcnt, m, hist);
-        if (lane == 0) atomicMax(&sm.pub[warp], km);
-    }
-    __syncwarp();
-    uint32_t mn = (lane < NWARPS) ? *reinterpret_cast<volatile uint32_t*>(&sm.pub[lane]) : 0xFFFFFFFFu;
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, d));
-    if (mn == 0u) {
-        if (wcnt >= k) {
-            const uint32_t kk = warp_select_kth(wk, wcnt, k, hist);
-            if (lane == 0) atomicMax(&sm.thr_key, kk);
-        }
-    } else if (lane == 0) {
-        atomicMax(&sm.thr_key, mn);
-    }
-    __syncwarp();
-    const uint32_t T = *reinterpret_cast<volatile uint32_t*>(&sm.thr_key);
-    wcnt = warp_compact_ge(wk, wi, wcnt, T);
-}
-
-__global__ void __launch_bounds__(NT_WS, 2) sample_kernel_ws(Params p) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    float* ring = reinterpret_cast<float*>(smem);
-    unsigned char* region = smem + RING_BYTES;
-    uint32_t* ckey = reinterpret_cast<uint32_t*>(region);
-    int32_t* cidx = reinterpret_cast<int32_t*>(region + CAP * 4);
-    Misc& sm = *reinterpret_cast<Misc*>(region + REGION_BYTES);
-    uint32_t* whist_all = reinterpret_cast<uint32_t*>(smem + SMEM_BYTES);
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31;
-    const int k = p.k_use;
-    const int64_t V = p.vocab;
-    const int64_t G = gridDim.x;
-    const int64_t nj = (p.units > (int64_t)blockIdx.x) ? (p.units - blockIdx.x + G - 1) / G : 0;
-    const int S = p.S, TPC = p.tiles_per_chunk;
-    const int64_t NTL = (V + TILE - 1) / TILE;
-    auto unit_tiles = [&](int64_t u) -> int {
-        const int64_t t0 = (int64_t)(u % S) * TPC;
-        return (int)min((int64_t)TPC, NTL - t0);
-    };
-
-    if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&sm.bar[s], 1);
-            mbar_init(&sm.ebar[s], NWARPS);
-        }
-        sm.flags = 0;
-        fence_mbar_init();
-    }
-    __syncthreads();
-
-    if (warp == NWARPS) {
-        // Producer warp: lane 0 streams every tile of every unit of this CTA.
-        if (lane == 0) {
-            const uint64_t pol = policy_evict_normal();
-            uint32_t seq = 0;
-            bool ok = true;
-            for (int64_t j = 0; j < nj && ok; ++j) {
-                const int64_t u = blockIdx.x + j * G;
-                const int64_t row = u / S;
-                const int nt = unit_tiles(u);
-                for (int t = 0; t < nt; ++t, ++seq) {
-                    const int s = seq % STAGES;
-                    if (seq >= STAGES && !mbar_wait_bounded(&sm.ebar[s], ((seq / STAGES) - 1) & 1)) {
-                        atomicOr(&sm.flags, FLAG_TIMEOUT);
-                        ok = false;
-                        break;
-                    }
-                    const int64_t a = ((int64_t)(u % S) * TPC + t) * TILE;
-                    const int64_t b = min(a + TILE, V);
-                    const uint32_t bytes = (uint32_t)(((b - a) & ~int64_t(3)) * 4);
-                    if (bytes) {
-                        mbar_arrive_expect_tx(&sm.bar[s], bytes);
-                        bulk_g2s(ring + s * TILE, p.logits + row * p.ld + a, bytes, &sm.bar[s], pol);
-                    } else {
-                        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.bar[s])) : "memory");
-                    }
-                }
-            }
-        }
-        return;
-    }
-
-    uint32_t* wk = ckey + warp * WCAP;
-    int32_t* wi = cidx + warp * WCAP;
-    uint32_t* whist = whist_all + warp * 256;
-    // shrink a warp buffer once it holds 2m entries (at least 32), m = ceil(k / NWARPS)
-    const int wtrig = min(WTRIG, max(2 * ((k + NWARPS - 1) / NWARPS), 32));
-    uint32_t cseq = 0;
-    MXS_PROF_BEGIN();
-    MXS_PROF_T0(ttot);
-    for (int64_t j = 0; j < nj; ++j) {
-        const int64_t u = blockIdx.x + j * G;
-        const int64_t row = u / S;
-        const int c = (int)(u % S);
-        const int nt = unit_tiles(u);
-        const float* xr = p.logits + row * p.ld;
-        csync();  // the previous unit is finished by every consumer thread
-        if (tid == 0) {
-            sm.cnt = 0;
-            sm.thr = -INFINITY;
-            sm.thr_key = 0u;  // below every key of a non-NaN logit
-            for (int w = 0; w < NWARPS; ++w) sm.pub[w] = 0u;
-            atomicAnd(&sm.flags, FLAG_TIMEOUT);  // a producer timeout stays; row flags start clear
-        }
-        csync();
-        int wcnt = 0, nan = 0, ntrig = wtrig;
-        bool stopped = false;
-        for (int t = 0; t < nt; ++t, ++cseq) {
-            const int64_t a = ((int64_t)c * TPC + t) * TILE;
-            const int len = (int)(min(a + TILE, V) - a);
-            const int bulk_n = len & ~3;
-            const int s = cseq % STAGES;
-            MXS_PROF_T0(tw);
-            if (!mbar_wait_bounded(&sm.bar[s], (cseq / STAGES) & 1)) atomicOr(&sm.flags, FLAG_TIMEOUT);
-            MXS_PROF_ADD(0, tw);
-            MXS_PROF_T0(tc);
-            const float* st = ring + s * TILE;
-            // this lane's 4 groups of 4 logits: float4 slots warp*128 + lane + 32q
-            float vv[16];
-            uint32_t valid = 0xFFFFu;
-            if (len == TILE) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 f = *reinterpret_cast<const float4*>(st + 4 * (warp * 128 + lane + 32 * q));
-                    vv[4 * q] = f.x; vv[4 * q + 1] = f.y; vv[4 * q + 2] = f.z; vv[4 * q + 3] = f.w;
-                }
-            } else {
-                valid = 0;
-#pragma unroll
-                for (int b = 0; b < 16; ++b) {
-                    const int e = 4 * (warp * 128 + lane + 32 * (b >> 2)) + (b & 3);
-                    vv[b] = -INFINITY;
-                    if (e < len) {
-                        vv[b] = (e < bulk_n) ? st[e] : xr[a + e];
-                        valid |= 1u << b;
-                    }
-                }
-            }
-            // Screen the 16 with one max.NaN reduction (missing slots hold -inf).
-            float mx8[8];
-#pragma unroll
-            for (int b = 0; b < 8; ++b) mx8[b] = fmax_nan(vv[2 * b], vv[2 * b + 1]);
-#pragma unroll
-            for (int b = 0; b < 4; ++b) mx8[b] = fmax_nan(mx8[2 * b], mx8[2 * b + 1]);
-            const float mxn = fmax_nan(fmax_nan(mx8[0], mx8[1]), fmax_nan(mx8[2], mx8[3]));
-            nan |= (mxn != mxn);
-            if (t == 0) {
-                // Seed: the k-th largest of the 256 per-lane maxima of the
-                // unit's first tile (k <= KWS distinct logits are >= it).
-                float mx = -INFINITY;
-#pragma unroll
-                for (int b = 0; b < 16; ++b) mx = vv[b] > mx ? vv[b] : mx;
-                ckey[tid] = fkey(mx);
-                csync();
-                const uint32_t kth = block_select_kth(ckey, NT, k, sm);
-                if (tid == 0) sm.thr_key = kth;
-                csync();
-            }
-            const float thr = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&sm.thr_key));
-            if (!stopped && __any_sync(0xffffffffu, mxn >= thr)) {
-                auto pass_bits = [&](float th) -> uint32_t {
-                    uint32_t m = 0;
-                    if (mxn >= th) {
-#pragma unroll
-                        for (int b = 0; b < 16; ++b)
-                            if (vv[b] >= th) m |= 1u << b;
-                    }
-                    return m & valid;
-                };
-                uint32_t m = pass_bits(thr);
-                int c = __popc(m);
-                int incl = warp_incl_scan(c);
-                int tot = __shfl_sync(0xffffffffu, incl, 31);
-                if (wcnt + tot > WCAP) {
-                    // does not fit: raise the bound and filter again; if it still
-                    // does not fit (massive ties) the exact replay takes the row
-                    warp_shrink(wk, wi, wcnt, k, whist, sm);
-                    const float thr2 = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&sm.thr_key));
-                    m = pass_bits(thr2);
-                    c = __popc(m);
-                    incl = warp_incl_scan(c);
-                    tot = __shfl_sync(0xffffffffu, incl, 31);
-                    if (wcnt + tot > WCAP) {
-                        stopped = true;
-                        m = 0;
-                        tot = 0;
-                        if (lane == 0) atomicOr(&sm.flags, FLAG_OVERFLOW);
-                    }
-                }
-                // append the passing logits, reading them back from the stage
-                int pos = wcnt + incl - c;
-                while (m) {
-                    const int b = __ffs(m) - 1;
-                    m &= m - 1;
-                    const int e = 4 * (warp * 128 + lane + 32 * (b >> 2)) + (b & 3);
-                    const float v = (e < bulk_n) ? st[e] : xr[a + e];
-                    wk[pos] = fkey(v);
-                    wi[pos] = (int32_t)(a + e);
-                    ++pos;
-                }
-                wcnt += tot;
-                if (wcnt > ntrig) {
-                    MXS_PROF_T0(ts);
-                    warp_shrink(wk, wi, wcnt, k, whist, sm);
-                    // hysteresis: if the bound has not caught up yet, let the
-                    // buffer grow before selecting again
-                    ntrig = min(WCAP - 64, max(wtrig, 2 * wcnt));
-                    MXS_PROF_ADD(2, ts);
-                }
-            }
-            // every lane of the warp is done with the stage: hand it back
-            __syncwarp();
-            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.ebar[s])) : "memory");
-            MXS_PROF_ADD(1, tc);
-        }
-        // Gather the warp buffers (entries >= the final bound) into ckey/cidx[0, cnt).
-        csync();
-        const uint32_t fin = sm.thr_key;
-        constexpr int PER = WCAP / 32;
-        uint32_t kk[PER];
-        int32_t ii[PER];
-        uint32_t keep = 0;
-#pragma unroll
-        for (int r = 0; r < PER; ++r) {
-            const int i = lane + 32 * r;
-            kk[r] = 0;
-            ii[r] = 0;
-            if (i < wcnt) {
-                kk[r] = wk[i];
-                ii[r] = wi[i];
-                if (kk[r] >= fin) keep |= 1u << r;
-            }
-        }
-        int total;
-        const int off = block_excl_scan(__popc(keep), sm, &total);  // (ends with a CTA sync)
-        int pos = off;
-#pragma unroll
-        for (int r = 0; r < PER; ++r) {
-            if (keep & (1u << r)) {
-                ckey[pos] = kk[r];
-                cidx[pos] = ii[r];
-                ++pos;
-            }
-        }
-        if (tid == 0) {
-            sm.cnt = total;
-            sm.thr = fkey_inv(fin);
-        }
-        const uint32_t flags = sm.flags | (csync_or(nan) ? FLAG_NAN : 0u);
-        MXS_PROF_T0(tf);
-        unit_end(p, row, c, flags, region, sm);
-        MXS_PROF_ADD(3, tf);
-    }
-    MXS_PROF_ADD(7, ttot);
-    MXS_PROF_FLUSH();
-}
-
-// ---------------------------------------------------------------------------
 // Host-side launch.
 // ---------------------------------------------------------------------------
 size_t sample_kernel_smem_bytes() { return SMEM_BYTES; }
@@ -782,21 +517,11 @@ cudaError_t sample_kernel_configure(int* blocks_per_sm) {
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(sample_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(sample_kernel_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES_WS);
-    if (e != cudaSuccess) return e;
-    int a = 0, b = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, sample_kernel<true>, NT, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, sample_kernel_ws, NT_WS, SMEM_BYTES_WS);
-    if (e != cudaSuccess) return e;
-    *blocks_per_sm = a < b ? a : b;
-    return cudaSuccess;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, sample_kernel<true>, NT, SMEM_BYTES);
 }
 
 cudaError_t sample_kernel_launch(const Params& p, int grid, bool tma, cudaStream_t stream) {
-    if (tma && p.mode != MODE_MERGE && p.k_use <= KWS && !p.force_block_path)
-        sample_kernel_ws<<<grid, NT_WS, SMEM_BYTES_WS, stream>>>(p);
-    else if (tma)
+    if (tma)
         sample_kernel<true><<<grid, NT, SMEM_BYTES, stream>>>(p);
     else
         sample_kernel<false><<<grid, NT, SMEM_BYTES, stream>>>(p);

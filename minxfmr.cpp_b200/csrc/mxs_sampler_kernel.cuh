@@ -70,8 +70,6 @@ struct Params {
     const uint32_t* in_count;  // MODE_MERGE: nshards x rows
     const uint32_t* in_flags;  // MODE_MERGE: nshards x rows (nullable)
     int nshards, in_cap;
-    int force_block_path;      // 1: use the CTA-synchronous streaming kernel even where the
-                               // warp-specialised one applies (tests cover both)
     // two-kernel path (k <= KSPLIT): stream -> per-row candidate lists -> finish (+ replay)
     uint64_t* row_cand;        // rows x row_cap, (key << 32) | column
     uint32_t* row_cnt;         // rows: entries appended (may exceed row_cap: overflow)
@@ -106,18 +104,13 @@ struct Misc {
     int xn;
     double sum;
     int32_t pick_next;
+    uint32_t dead;          // a bounded wait ran out: no more copies are issued
 };
 constexpr size_t RING_BYTES = size_t(STAGES) * TILE * sizeof(float);
 constexpr size_t REGION_BYTES = size_t(CAP) * 8;
 constexpr size_t SMEM_BYTES = RING_BYTES + REGION_BYTES + sizeof(Misc);
-// Warp-specialised variant: 8 consumer warps + 1 producer warp; each consumer
-// warp owns WCAP entries of the candidate region and a 256-bin histogram.
-constexpr int KWS = 128;                 // largest k of the warp-specialised path
+// The streaming kernel of the two-kernel path: 8 consumer warps + 1 producer warp.
 constexpr int NT_WS = NT + 32;
-constexpr int WCAP = CAP / NWARPS;       // 512 candidates per warp
-constexpr int WTRIG = WCAP / 2;          // shrink a warp buffer past this
-constexpr size_t WHIST_BYTES = size_t(NWARPS) * 256 * 4;
-constexpr size_t SMEM_BYTES_WS = SMEM_BYTES + WHIST_BYTES;
 static_assert(SORTMAX * 8 + KFAST * 8 <= REGION_BYTES, "sort + prob buffers exceed the region");
 static_assert(HEAP_SMEM_MAX * 8 + XTILE * 8 <= REGION_BYTES, "heap + replay list exceed the region");
 

@@ -38,6 +38,7 @@ struct StreamSmem {
     uint64_t full[S_STAGES];
     uint64_t empty[S_STAGES];
     UnitState us[SLOTS];
+    uint32_t dead;  // a bounded wait ran out: the producer issues no more copies
 };
 
 constexpr size_t S_RING = size_t(S_STAGES) * S_TILE * 4;
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], NWARPS);
         }
+        sm.dead = 0u;
         for (int i = 0; i < SLOTS; ++i) {
             sm.us[i].thr_key = 0u;
             sm.us[i].done = 0u;
@@ -141,20 +143,26 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
     if (warp == NWARPS) {  // producer
         if (lane == 0) {
             const uint64_t pol = policy_evict_normal();
-            uint32_t seq = 0;
-            for (int64_t j = 0; j < nj; ++j) {
+            volatile uint32_t* dead = &sm.dead;
+            uint32_t seq = 0;  // copies issued (tiles)
+            bool stop = false;
+            for (int64_t j = 0; j < nj && !stop; ++j) {
                 const int64_t u = blockIdx.x + j * G;
                 const int64_t row = u / S;
                 const int nt = unit_tiles(u);
-                for (int t = 0; t < nt; ++t, ++seq) {
+                for (int t = 0; t < nt; ++t) {
                     const int s = seq % S_STAGES;
-                    // Test hook: stop issuing (every earlier copy has been
-                    // waited for by the consumers, so none is left in flight);
-                    // the consumers' bounded wait then runs out.
-                    if (blockIdx.x == 0 && (int64_t)seq == p.debug_drop_tile) return;
+                    // A consumer's wait ran out, or (test hook) CTA 0 stops
+                    // before this tile: issue nothing more.
+                    if (*dead || (blockIdx.x == 0 && (int64_t)seq == p.debug_drop_tile)) {
+                        stop = true;
+                        break;
+                    }
                     if (seq >= S_STAGES && !mbar_wait_bounded(&sm.empty[s], ((seq / S_STAGES) - 1) & 1)) {
                         atomicOr(&p.row_flag[row], FLAG_TIMEOUT);
-                        return;  // consumers time out on the stages that never come
+                        *dead = 1u;
+                        stop = true;
+                        break;  // consumers time out on the stages that never come
                     }
                     const int64_t a = ((int64_t)(u % S) * TPC + t) * S_TILE;
                     const int64_t b = min(a + S_TILE, V);
@@ -165,8 +173,15 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                     } else {
                         asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.full[s])) : "memory");
                     }
+                    ++seq;
                 }
             }
+            // Before the CTA can retire, every copy this thread issued must have
+            // landed: consumers that gave up no longer wait for them. Only the
+            // last S_STAGES copies can still be in flight (each stage's earlier
+            // phases were waited for through `empty`); each wait is bounded.
+            for (uint32_t q = seq > S_STAGES ? seq - S_STAGES : 0; q < seq; ++q)
+                (void)mbar_wait_bounded(&sm.full[q % S_STAGES], (q / S_STAGES) & 1);
         }
         return;
     }
@@ -214,9 +229,14 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             const int a = a0 + t * S_TILE;
             const int len = (t == nt - 1) ? last_len : S_TILE;
             const int bulk_n = len & ~3;
+            if (!dead && *reinterpret_cast<volatile uint32_t*>(&sm.dead)) {
+                fl |= FLAG_TIMEOUT;  // another warp's wait ran out: no more copies come
+                dead = true;
+            }
             if (!dead && !mbar_wait_bounded(&sm.full[s], parity)) {
                 fl |= FLAG_TIMEOUT;
                 dead = true;
+                *reinterpret_cast<volatile uint32_t*>(&sm.dead) = 1u;
             }
             const float* st = ring + s * S_TILE;
             float vv[32];

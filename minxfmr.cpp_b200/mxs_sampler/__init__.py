@@ -38,7 +38,7 @@ EXPORTS = (
     "mxs_sample_topk", "mxs_sample_topk_ex", "mxs_workspace_size", "mxs_workspace_init",
     "mxs_sample_topk_host", "mxs_shard_candidates", "mxs_merge_sample", "mxs_get_status",
     "mxs_version", "mxs_sample_topk_noalloc", "mxs_set_profile_events", "mxs_sample_rowsharded",
-    "mxs_sample_vocabsharded",
+    "mxs_sample_vocabsharded", "mxs_set_test_hooks",
 )
 
 _P = ctypes.c_void_p
@@ -61,6 +61,7 @@ _SIGS = {
     "mxs_sample_rowsharded": [_P, _I64, _I, _I, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P,
                               ctypes.POINTER(_I64), _P],
     "mxs_sample_vocabsharded": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _P, _P],
+    "mxs_set_test_hooks": [_I64, _I, _I],
 }
 
 _lib = None
@@ -321,6 +322,16 @@ def set_profile_events(start=None, stop=None):
     sp = None if start is None else ctypes.c_void_p(start.cuda_event)
     ep = None if stop is None else ctypes.c_void_p(stop.cuda_event)
     _check("mxs_set_profile_events", load().mxs_set_profile_events(sp, ep))
+
+
+PATH_DEFAULT = 0
+PATH_BLOCK = 2
+
+
+def set_test_hooks(drop_tile=-1, replay_warp_min=2, path=PATH_DEFAULT):
+    """Test hooks of this library's tests (mxs_set_test_hooks); the defaults
+    turn every hook off."""
+    _check("mxs_set_test_hooks", load().mxs_set_test_hooks(int(drop_tile), int(replay_warp_min), int(path)))
 
 
 def get_status(clear=True):

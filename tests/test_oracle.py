@@ -48,10 +48,56 @@ def golden_logits(c):
     return x
 
 
+def truncated_probs(p, top_p, min_p):
+    """The reference's top-p then min-p truncation with renormalisation
+    (src/api/minxfmr.cpp:2104-2111 clamps, :2128-2165), applied to one row's
+    first-normalised probabilities p[0, k) with the same double operations in
+    the same order (Python floats are IEEE doubles). Returns the whole vector
+    as the reference leaves it (the kept prefix renormalised in place, the rest
+    untouched) and the kept count."""
+    if top_p <= 0.0 or top_p > 1.0:
+        top_p = 1.0
+    min_p = min(max(min_p, 0.0), 1.0)
+    q = [float(v) for v in p]
+    n = len(q)
+    if top_p < 1.0:
+        cum, n = 0.0, 0
+        for i in range(len(q)):
+            cum += q[i]
+            n = i + 1
+            if cum >= top_p:
+                break
+        n = max(n, 1)
+        renorm = 0.0
+        for i in range(n):
+            renorm += q[i]
+        if renorm > 0.0:
+            for i in range(n):
+                q[i] /= renorm
+    if min_p > 0.0 and n > 1:
+        thr = q[0] * min_p
+        keep = 1
+        for i in range(1, n):
+            if q[i] >= thr:
+                keep = i + 1
+            else:
+                break
+        n = keep
+        renorm = 0.0
+        for i in range(n):
+            renorm += q[i]
+        if renorm > 0.0:
+            for i in range(n):
+                q[i] /= renorm
+    return np.array(q), n
+
+
 def check_against_golden(c, nxt, idx, prob):
-    """Compare sampler outputs with a golden case (ids and order bit-exact,
-    probabilities within 1e-6 relative where the reference's probs vector is
-    the first-normalised one: top_p = 1 and min_p = 0 and not greedy)."""
+    """Compare sampler outputs with a golden case: ids and order bit-exact;
+    probabilities within 1e-6 relative. The reference's probs vector is the
+    first-normalised one when top_p = 1 and min_p = 0; otherwise it is the
+    truncated, renormalised one, which the sampler's first-normalised output
+    must reproduce through the reference's truncation steps."""
     import hashlib
     np.testing.assert_array_equal(nxt, c["next"], err_msg=c["name"])
     if "idx" in c:
@@ -63,9 +109,14 @@ def check_against_golden(c, nxt, idx, prob):
     got = prob[:, :ref_prob.shape[1]]
     neutral = c["top_p"] >= 1.0 and c["min_p"] <= 0.0
     for r in range(len(nxt)):
-        if c["plen"][r] > 0 and neutral:
-            np.testing.assert_allclose(got[r, :c["plen"][r]], ref_prob[r, :c["plen"][r]], rtol=1e-6, atol=0,
-                                       err_msg=c["name"])
+        n = int(c["plen"][r])
+        if n <= 0:
+            continue
+        if neutral:
+            np.testing.assert_allclose(got[r, :n], ref_prob[r, :n], rtol=1e-6, atol=0, err_msg=c["name"])
+        elif "prob" in c:
+            t, _ = truncated_probs(prob[r], c["top_p"], c["min_p"])
+            np.testing.assert_allclose(t[:n], ref_prob[r, :n], rtol=1e-6, atol=0, err_msg=c["name"])
 
 
 GOLDEN_CASES = load_golden()
