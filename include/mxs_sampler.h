@@ -211,7 +211,7 @@ MXS_API int mxs_sample_topk_noalloc(const float* d_logits, int64_t rows, int64_t
  *                    sequence number, so its consumers' bounded wait runs out and
  *                    the rows report MXS_ROW_TIMEOUT (-1: off, the default)
  *   replay_warp_min  a finish CTA replays its tie rows one per warp when it holds
- *                    at least this many, else with the whole CTA (default 2)
+ *                    at least this many, else with the whole CTA (default 1)
  *   path             0: default planning; 2: the CTA-synchronous kernel for every k
  * Process-wide; calls already enqueued keep the hooks they were launched with.
  */

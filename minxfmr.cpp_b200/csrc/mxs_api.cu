@@ -83,7 +83,7 @@ struct Plan {
     int k_use = 1;
     int S = 1, tpc = 1, grid = 1, outcap = 0;
     bool split = false;  // two-kernel path (stream -> finish, which also replays tie rows)
-    size_t off_rcand = 0, off_rcnt = 0, off_rflag = 0, zero_bytes = 0;
+    size_t off_rcand = 0, off_rcnt = 0, off_rflag = 0, off_rbound = 0, zero_bytes = 0;
     int64_t units = 0;
     size_t off_counter = 0, off_state = 0, off_status = 0, off_ccount = 0, off_cand = 0, off_heap = 0,
            off_prob = 0, total = 0;
@@ -100,7 +100,7 @@ int clamp_k(int top_k, int64_t vocab) {
 // can change what a sampling call does.
 struct TestHooks {
     int64_t drop_tile = -1;     // CTA 0's streaming producer stops before this tile (-1: off)
-    int replay_warp_min = 2;    // tie rows of a finish CTA replayed one per warp from this many
+    int replay_warp_min = 1;    // tie rows of a finish CTA replayed one per warp from this many
     int path = 0;               // 0: default planning; 2: the CTA-synchronous kernel for every k
 };
 TestHooks g_hooks;
@@ -109,9 +109,12 @@ TestHooks g_hooks;
 // rows, unless a test forced the CTA-synchronous kernel.
 int path_override() { return g_hooks.path; }
 
-// Candidate list entries per row: a row split over S chunks gets up to 256 per
-// chunk (each chunk keeps at least k of its own logits).
-int split_row_cap(int S) { return std::max(mxs::SPLIT_ROW_CAP, 256 * S); }
+// Candidate list entries per row on the two-kernel path: per chunk, the first
+// tile's candidates (about 2k) and the would-enter superset of the later tiles
+// (about k (1 + ln(tiles))); measured lists of N(0, 2^2) rows at V = 151,936
+// hold ~420 entries at k = 50 and ~900 at k = 128. A fuller list overflows and
+// the row is replayed from its full logits.
+int split_row_cap(int S, int k) { return S * std::max(mxs::SPLIT_ROW_CAP, 12 * k + 512); }
 
 bool use_split(int64_t vocab, int64_t ld, const float* logits, int k_use) {
     const bool tma = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && (ld % 4 == 0);
@@ -165,10 +168,11 @@ Plan make_plan(const Device& d, int64_t rows, int64_t vocab, int k_use, bool mer
         // finish kernel clears them after use
         pl.off_rcnt = o;
         pl.off_rflag = pl.off_rcnt + sizeof(uint32_t) * (size_t)rows;
-        pl.zero_bytes = 2 * sizeof(uint32_t) * (size_t)rows;
-        o = align_up(pl.off_rflag + sizeof(uint32_t) * (size_t)rows, 256);
+        pl.off_rbound = pl.off_rflag + sizeof(uint32_t) * (size_t)rows;
+        pl.zero_bytes = 3 * sizeof(uint32_t) * (size_t)rows;
+        o = align_up(pl.off_rbound + sizeof(uint32_t) * (size_t)rows, 256);
         pl.off_rcand = o;
-        o = align_up(o + sizeof(uint64_t) * (size_t)rows * split_row_cap(pl.S), 256);
+        o = align_up(o + sizeof(uint64_t) * (size_t)rows * split_row_cap(pl.S, pl.k_use), 256);
     } else if (pl.S > 1) {
         o = align_up(o + sizeof(uint32_t) * (size_t)rows * pl.S, 256);
         pl.off_cand = o;
@@ -214,7 +218,8 @@ void fill_workspace(Params& p, const Plan& pl, void* ws, const Device& d) {
         p.row_cand = reinterpret_cast<uint64_t*>(b + pl.off_rcand);
         p.row_cnt = reinterpret_cast<uint32_t*>(b + pl.off_rcnt);
         p.row_flag = reinterpret_cast<uint32_t*>(b + pl.off_rflag);
-        p.row_cap = split_row_cap(pl.S);
+        p.row_bound = reinterpret_cast<uint32_t*>(b + pl.off_rbound);
+        p.row_cap = split_row_cap(pl.S, pl.k_use);
     }
 }
 

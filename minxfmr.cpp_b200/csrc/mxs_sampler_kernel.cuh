@@ -74,6 +74,8 @@ struct Params {
     uint64_t* row_cand;        // rows x row_cap, (key << 32) | column
     uint32_t* row_cnt;         // rows: entries appended (may exceed row_cap: overflow)
     uint32_t* row_flag;        // rows: OR of FLAG_* seen while streaming
+    uint32_t* row_bound;       // rows: key of a lower bound of the row's k-th largest logit, from the
+                               // streaming warps (0: none); cleared by the finish kernel
     int row_cap;
     int replay_warp_min;       // the finish kernel replays tie rows one per warp when its CTA holds at
                                // least this many of them, else with the whole CTA (MXS_REPLAY_WARP_MIN)

@@ -328,7 +328,7 @@ PATH_DEFAULT = 0
 PATH_BLOCK = 2
 
 
-def set_test_hooks(drop_tile=-1, replay_warp_min=2, path=PATH_DEFAULT):
+def set_test_hooks(drop_tile=-1, replay_warp_min=1, path=PATH_DEFAULT):
     """Test hooks of this library's tests (mxs_set_test_hooks); the defaults
     turn every hook off."""
     _check("mxs_set_test_hooks", load().mxs_set_test_hooks(int(drop_tile), int(replay_warp_min), int(path)))
