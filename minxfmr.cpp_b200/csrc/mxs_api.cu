@@ -111,9 +111,9 @@ int path_override() { return g_hooks.path; }
 
 // Candidate list entries per row on the two-kernel path: per chunk, the first
 // tile's candidates (about 2k) and the would-enter superset of the later tiles
-// (about k (1 + ln(tiles))); measured lists of N(0, 2^2) rows at V = 151,936
-// hold ~420 entries at k = 50 and ~900 at k = 128. A fuller list overflows and
-// the row is replayed from its full logits.
+// (about k (1 + ln(tiles))); a simulation of the bound on N(0, 2^2) rows at
+// V = 151,936 gives ~420 entries at k = 50 and ~900 at k = 128. A fuller list
+// overflows and the row is replayed from its full logits.
 int split_row_cap(int S, int k) { return S * std::max(mxs::SPLIT_ROW_CAP, 12 * k + 512); }
 
 bool use_split(int64_t vocab, int64_t ld, const float* logits, int k_use) {

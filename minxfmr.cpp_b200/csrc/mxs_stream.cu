@@ -16,6 +16,14 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#ifdef MXS_PROFILE
+// Counters of the per-warp replays (profiling build): replays, heap build,
+// first-tile reads, list windows, final sort, draw (cycles summed over
+// replays).
+namespace mxs {
+__device__ unsigned long long g_rep_prof[8];
+}
+#endif
 #include "mxs_rowfinish.cuh"
 #include "mxs_stream.h"
 
@@ -494,9 +502,11 @@ constexpr int F_WARPS = 8;
 struct FinishWarpSmem {
     uint32_t keys[FCAP];
     int32_t idx[FCAP];
-    uint32_t hist[256];
     double pbuf[KSPLIT_K];
     Ent e[KSPLIT_K];
+    // the replay's heap: values and indices, 1-based (soa_* in mxs_heap.cuh)
+    alignas(8) float hv[KSPLIT_K + 2];
+    alignas(8) int32_t hi[KSPLIT_K + 2];
 };
 
 // Draws for row `row` from e[0, k) and writes next (and the optional outputs);
@@ -614,9 +624,6 @@ __device__ __forceinline__ void xload4(const float* x, int64_t j, int64_t V, flo
 }
 
 #ifdef MXS_PROFILE
-// Phase clocks of the per-warp replays (profiling build): replays, heap build,
-// first-tile reads, list windows, final sort, draw (cycles summed over replays).
-__device__ unsigned long long g_rep_prof[8];
 #define MXS_REP_T(v) long long v = clock64()
 #define MXS_REP_ADD(i, x) do { if (lane == 0) atomicAdd(&g_rep_prof[i], (unsigned long long)(x)); } while (0)
 extern "C" __attribute__((visibility("default"))) int mxs_prof_read_rep(unsigned long long* host, int clear) {
@@ -639,9 +646,8 @@ extern "C" __attribute__((visibility("default"))) int mxs_prof_read_rep(unsigned
 // another quarter step. The root only rises (no NaN), so a stale root lets
 // through a superset of the logits that enter, and each offer makes the exact
 // comparison itself. Returns the root (in every lane).
-template <bool LOOKAHEAD>
-__device__ __noinline__ float warp_replay_range(const float* x, int64_t V, int64_t lo, int64_t hi, Ent* h, int k, Ent* slot,
-                                   float r0) {
+__device__ __noinline__ float warp_replay_range(const float* x, int64_t V, int64_t lo, int64_t hi, SoaHeap h,
+                                                int k, Ent* slot, float r0) {
     const int lane = threadIdx.x & 31;
     if (lo >= hi) return r0;
     int c = 0;
@@ -665,7 +671,11 @@ __device__ __noinline__ float warp_replay_range(const float* x, int64_t V, int64
         for (int q = 0; q < 4; ++q) {
             if (c > XSLOT - 128) {
                 __syncwarp();
-                if (lane == 0) r0 = heap_offer_list_top<LOOKAHEAD>(h, k, slot, c, r0);
+                MXS_REP_T(o0);
+                if (lane == 0) r0 = soa_offer_list(h, k, slot, c, r0);
+                MXS_REP_T(o1);
+                MXS_REP_ADD(6, o1 - o0);
+                MXS_REP_ADD(7, c);
                 r0 = __shfl_sync(0xffffffffu, r0, 0);
                 c = 0;
             }
@@ -685,7 +695,11 @@ __device__ __noinline__ float warp_replay_range(const float* x, int64_t V, int64
         }
     }
     __syncwarp();
-    if (lane == 0) r0 = heap_offer_list_top<LOOKAHEAD>(h, k, slot, c, r0);
+    MXS_REP_T(o0);
+    if (lane == 0) r0 = soa_offer_list(h, k, slot, c, r0);
+    MXS_REP_T(o1);
+    MXS_REP_ADD(6, o1 - o0);
+    MXS_REP_ADD(7, c);
     return __shfl_sync(0xffffffffu, r0, 0);
 }
 
@@ -693,9 +707,8 @@ __device__ __noinline__ float warp_replay_range(const float* x, int64_t V, int64
 // root, in column order: windows of at most LWIN entries (halved until they
 // fit), each gathered into `slot`, sorted by column in registers and offered.
 constexpr int LWIN = 128;
-template <bool LOOKAHEAD>
-__device__ __noinline__ float warp_replay_list(const uint64_t* list, int n, int64_t lo, int64_t hi, Ent* h, int k, Ent* slot,
-                                  float r0) {
+__device__ __noinline__ float warp_replay_list(const uint64_t* list, int n, int64_t lo, int64_t hi, SoaHeap h,
+                                               int k, Ent* slot, float r0) {
     const int lane = threadIdx.x & 31;
     const uint32_t lt = (1u << lane) - 1u;
     while (lo < hi) {
@@ -741,7 +754,7 @@ __device__ __noinline__ float warp_replay_list(const uint64_t* list, int n, int6
                 if (i < c) slot[i] = Ent{__uint_as_float((uint32_t)b[q]), (int32_t)~(uint32_t)(b[q] >> 32)};
             }
             __syncwarp();
-            if (lane == 0) r0 = heap_offer_list_top<LOOKAHEAD>(h, k, slot, c, r0);
+            if (lane == 0) r0 = soa_offer_list(h, k, slot, c, r0);
             r0 = __shfl_sync(0xffffffffu, r0, 0);
         }
         lo = whi;
@@ -751,52 +764,56 @@ __device__ __noinline__ float warp_replay_list(const uint64_t* list, int n, int6
 
 // One warp replays the reference's partial_sort heap process over row `row`
 // without reading the whole row again, and draws. Rows without NaN, k <=
-// KSPLIT_K, whose list did not overflow. The heap lives in w.e; w.keys/w.idx
-// hold the replay list. A row is streamed as S chunks of TPC tiles; in each
-// chunk the logits of the first tile are read again from memory, and those of
-// the later tiles come from the row's list, which holds every one of them that
-// is strictly above a lower bound of the k-th largest logit before it within
-// the chunk -- so every logit that can enter the heap (the reference enters
-// logit i only if it is strictly above the k-th largest of x[0, i)), in the
-// chunk's order.
-template <bool LOOKAHEAD>
+// KSPLIT_K, whose list did not overflow. The heap lives in w.hv / w.hi; w.keys
+// / w.idx hold the replay list. A row is streamed as S chunks of TPC tiles; in
+// each chunk the logits of the first tile are read again from memory, and
+// those of the later tiles come from the row's list, which holds every one of
+// them that is strictly above a lower bound of the k-th largest logit before
+// it within the chunk -- so every logit that can enter the heap (the
+// reference enters logit i only if it is strictly above the k-th largest of
+// x[0, i)), in the chunk's order.
 __device__ void exact_row_warp_log(const Params& p, int64_t row, FinishWarpSmem& w, uint32_t cnt_all) {
     const int lane = threadIdx.x & 31;
     const int k = p.k_use;
     const int64_t V = p.vocab;
     const float* x = p.logits + row * p.ld;
     const uint64_t* list = p.row_cand + row * (int64_t)p.row_cap;
-    Ent* h = w.e;
+    const SoaHeap h{w.hv, w.hi};
     Ent* slot = reinterpret_cast<Ent*>(w.keys);
     MXS_REP_T(q0);
-    for (int i = lane; i < k; i += 32) h[i] = Ent{x[i], i};
+    for (int i = lane; i < k; i += 32) {
+        w.hv[i + 1] = x[i];
+        w.hi[i + 1] = i;
+    }
     __syncwarp();
-    if (lane == 0) heap_build(h, k);
+    if (lane == 0) soa_build(h, k);
     __syncwarp();
     MXS_REP_T(q1);
     MXS_REP_ADD(0, 1);
     MXS_REP_ADD(1, q1 - q0);
-    float r0 = h[0].v;
+    float r0 = w.hv[1];
     const int64_t chunk = (int64_t)p.tiles_per_chunk * S_TILE;
     for (int c = 0; c < p.S; ++c) {
         const int64_t c0 = c * chunk;
         if (c0 >= V) break;
         const int64_t t1 = min(V, c0 + S_TILE), ce = min(V, c0 + chunk);
         MXS_REP_T(q2);
-        r0 = warp_replay_range<LOOKAHEAD>(x, V, max(c0, (int64_t)k), t1, h, k, slot, r0);
+        r0 = warp_replay_range(x, V, max(c0, (int64_t)k), t1, h, k, slot, r0);
         __syncwarp();
         MXS_REP_T(q3);
-        r0 = warp_replay_list<LOOKAHEAD>(list, (int)cnt_all, t1, ce, h, k, slot, r0);
+        r0 = warp_replay_list(list, (int)cnt_all, t1, ce, h, k, slot, r0);
         __syncwarp();
         MXS_REP_T(q4);
         MXS_REP_ADD(2, q3 - q2);
         MXS_REP_ADD(3, q4 - q3);
     }
     MXS_REP_T(q5);
-    if (lane == 0) heap_sort_top<LOOKAHEAD>(h, k);
+    if (lane == 0) soa_sort(h, k);
+    __syncwarp();
+    for (int i = lane; i < k; i += 32) w.e[i] = Ent{w.hv[i + 1], w.hi[i + 1]};
     __syncwarp();
     MXS_REP_T(q6);
-    warp_draw(p, row, h, k, w.pbuf);
+    warp_draw(p, row, w.e, k, w.pbuf);
     __syncwarp();
     MXS_REP_T(q7);
     MXS_REP_ADD(4, q6 - q5);
@@ -1068,10 +1085,7 @@ __global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) 
     csync();
     const bool by_warp = s_wn >= p.replay_warp_min;
     if (by_warp && need && !full) {
-        if (s_wn == 1)  // a lone replay: two heap levels per shared-memory round trip
-            exact_row_warp_log<true>(p, row, w, cnt_all);
-        else
-            exact_row_warp_log<false>(p, row, w, cnt_all);
+        exact_row_warp_log(p, row, w, cnt_all);
     }
     if (lane == 0 && need && (full || !by_warp)) {
         const int at = atomicAdd(&s_xn, 1);
