@@ -115,8 +115,12 @@ MXS_API int mxs_sample_topk_host(const float* h_logits, int64_t rows, int64_t vo
  * (order-preserving key << 32 | global column) words, at
  * d_cand + r*cap, with its length in d_count[r]; d_flags[r] gets MXS_ROW_NAN /
  * MXS_ROW_OVERFLOW when the list cannot stand for the shard (then the row
- * must be sampled from its full logits). col_offset is the shard's first
- * global column. cap >= k_use.
+ * must be sampled from its full logits). On the two-kernel path (top_k <= 128,
+ * 16-byte aligned rows) the list holds the logits above the k-th largest first,
+ * then those equal to it; when more of those tie than the list holds, it keeps
+ * as many as fit and d_flags[r] gets MXS_ROW_EXACT (every logit left out equals
+ * the list's smallest value; mxs_merge_sample accounts for it). col_offset is
+ * the shard's first global column. cap >= k_use.
  */
 MXS_API int mxs_shard_candidates(const float* d_shard_logits, int64_t rows, int64_t shard_cols, int64_t ld,
                          int64_t col_offset, int top_k, int cap, uint64_t* d_cand, uint32_t* d_count,
@@ -126,10 +130,13 @@ MXS_API int mxs_shard_candidates(const float* d_shard_logits, int64_t rows, int6
  * Vocab-sharded sampling, step 2, after the shards' lists are gathered (e.g. by
  * an NCCL all-gather) as nshards consecutive blocks of [rows x cap] words
  * (d_cand_all) and [rows] counts and flags. Merges each row's lists, selects
- * the top-k, and draws. Rows whose merge shows a tie, or whose shard flags are
- * set, are not drawn: their d_row_flags entry gets MXS_ROW_EXACT and d_next -1,
- * and the caller samples them with mxs_sample_topk_ex on the full row (the tie
- * order depends on every logit of the row).
+ * the top-k, and draws. Not drawn, with d_row_flags MXS_ROW_EXACT (plus the
+ * shard's MXS_ROW_NAN / MXS_ROW_OVERFLOW) and d_next -1: rows with a flagged
+ * shard list, rows whose truncated list (MXS_ROW_EXACT from
+ * mxs_shard_candidates) could hide some of the k largest, and tie rows whose
+ * order matters (top-k list requested, or a draw landing on a tied position).
+ * The caller samples them with mxs_sample_topk_ex on the full row (the tie
+ * order depends on every logit of the row), or as mxs_sample_vocabsharded does.
  */
 MXS_API int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count_all, const uint32_t* d_flags_all,
                      int nshards, int cap, int64_t rows, int64_t vocab, double temperature, int top_k,
@@ -157,18 +164,33 @@ MXS_API int mxs_sample_rowsharded(const float* d_local_logits, int64_t global_ro
  * passes the same rows: its column shard [rank*shard_cols, (rank+1)*shard_cols)
  * of a vocabulary of world*shard_cols, and the same d_u. Runs
  * mxs_shard_candidates, one NCCL all-gather group of the lists, and
- * mxs_merge_sample on the given stream; rows whose merged lists show a tie are
- * then gathered whole (one more all-gather) and sampled as full rows, so every
- * rank ends with the same outputs for every row, equal to mxs_sample_topk_ex
- * on the full rows. Synchronises the stream once, to learn how many rows need
- * the full-row pass. d_row_flags (nullable) gets MXS_ROW_EXACT on those rows.
- * Above top_k = 2048 (the merge's limit) every row takes the full-row pass.
- * Returns MXS_ERR_COMM when NCCL is not loaded or a collective fails.
+ * mxs_merge_sample on the given stream, so every rank ends with the same
+ * outputs for every row, equal to mxs_sample_topk_ex on the full rows. Rows
+ * whose merged lists show a tie that matters (their tie order depends on
+ * logits no list holds) are resolved from lists too, when top_k <= 128 and
+ * top_k <= shard_cols: rank 0 replays the reference's heap process over its
+ * shard and every later rank lists the logits of its shard that can still
+ * enter the heap; one more all-gather group, and every rank finishes the
+ * replay. Rows that lists cannot resolve (a NaN, a list over its capacity, a
+ * larger top_k) are gathered whole (one more all-gather) and sampled as full
+ * rows. Synchronises the stream once to learn how many rows were handed back,
+ * and once more when any were. d_row_flags (nullable) gets MXS_ROW_EXACT on
+ * the handed-back rows. Above top_k = 2048 (the merge's limit) every row is
+ * gathered whole. Calls on one device must not overlap (one lock per device;
+ * ranks on different devices never wait for each other's lock). Returns
+ * MXS_ERR_COMM when NCCL is not loaded or a collective fails.
  */
 MXS_API int mxs_sample_vocabsharded(const float* d_shard_logits, int64_t rows, int64_t shard_cols, int64_t ld,
                                     double temperature, int top_k, double top_p, double min_p, const double* d_u,
                                     int32_t* d_next, int32_t* d_topk_idx, double* d_topk_prob,
                                     uint32_t* d_row_flags, void* nccl_comm, void* stream);
+
+/*
+ * Measurement hook (no counterpart in the reference): rows of the last
+ * mxs_sample_vocabsharded call on the current device whose ties were resolved
+ * from lists, and rows that were gathered whole. Either pointer may be NULL.
+ */
+MXS_API int mxs_vocabsharded_stats(int64_t* tie_rows_from_lists, int64_t* rows_gathered_whole);
 
 /*
  * Measurement hook (no counterpart in the reference): when set, the next

@@ -276,6 +276,49 @@ int workspace_zero_prefix(size_t* bytes) {
     *bytes = make_plan(*d, 1, 1, 1, false).off_ccount;
     return MXS_OK;
 }
+
+int shard_step(const float* d_shard_logits, int64_t rows, int64_t shard_cols, int64_t ld, int64_t col_offset,
+               int top_k, int cap, uint64_t* d_cand, uint32_t* d_count, uint32_t* d_flags, uint32_t* d_log_count,
+               void* stream, ShardLog* log) {
+    if (rows < 0 || shard_cols <= 0 || ld < shard_cols || col_offset < 0 || col_offset + shard_cols > INT32_MAX)
+        return MXS_ERR_INVALID;
+    if (rows == 0) return MXS_OK;
+    if (!d_shard_logits || !d_cand || !d_count || !d_flags) return MXS_ERR_INVALID;
+    const int k_use = clamp_k(top_k, shard_cols);
+    if (cap < k_use) return MXS_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Device* d;
+    int rc = current_device(&d);
+    if (rc) return rc;
+    // k <= KSPLIT on 16-byte aligned rows: the two-kernel path, whose finish
+    // kernel writes the lists (MODE_EMIT); otherwise the CTA kernels.
+    const Plan pl = make_plan(*d, rows, shard_cols, k_use, false, use_split(shard_cols, ld, d_shard_logits, k_use));
+    rc = ensure_library_ws(*d, pl.total, (cudaStream_t)stream);
+    if (rc) return rc;
+    Params p{};
+    p.logits = d_shard_logits;
+    p.rows = rows;
+    p.vocab = shard_cols;
+    p.ld = ld;
+    p.k_use = k_use;
+    p.mode = mxs::MODE_EMIT;
+    p.col_offset = col_offset;
+    p.out_cand = d_cand;
+    p.out_count = d_count;
+    p.out_flags = d_flags;
+    p.out_cap = cap;
+    p.log_count = pl.split ? d_log_count : nullptr;
+    d->clean_rows = -1;
+    fill_workspace(p, pl, d->ws, *d);
+    if (log) {
+        log->valid = pl.split && d_log_count != nullptr;
+        log->cand = p.row_cand;
+        log->cap = p.row_cap;
+        log->S = pl.S;
+        log->tpc = pl.tpc;
+    }
+    return launch(p, pl, (cudaStream_t)stream);
+}
 }  // namespace mxs
 
 extern "C" {
@@ -412,36 +455,8 @@ int mxs_sample_topk_host(const float* h_logits, int64_t rows, int64_t vocab, int
 int mxs_shard_candidates(const float* d_shard_logits, int64_t rows, int64_t shard_cols, int64_t ld,
                          int64_t col_offset, int top_k, int cap, uint64_t* d_cand, uint32_t* d_count,
                          uint32_t* d_flags, void* stream) {
-    if (rows < 0 || shard_cols <= 0 || ld < shard_cols || col_offset < 0 || col_offset + shard_cols > INT32_MAX)
-        return MXS_ERR_INVALID;
-    if (rows == 0) return MXS_OK;
-    if (!d_shard_logits || !d_cand || !d_count || !d_flags) return MXS_ERR_INVALID;
-    const int k_use = clamp_k(top_k, shard_cols);
-    if (cap < k_use) return MXS_ERR_INVALID;
-    std::lock_guard<std::mutex> lk(g_mu);
-    Device* d;
-    int rc = current_device(&d);
-    if (rc) return rc;
-    // k <= KSPLIT on 16-byte aligned rows: the two-kernel path, whose finish
-    // kernel writes the lists (MODE_EMIT); otherwise the CTA kernels.
-    const Plan pl = make_plan(*d, rows, shard_cols, k_use, false, use_split(shard_cols, ld, d_shard_logits, k_use));
-    rc = ensure_library_ws(*d, pl.total, (cudaStream_t)stream);
-    if (rc) return rc;
-    Params p{};
-    p.logits = d_shard_logits;
-    p.rows = rows;
-    p.vocab = shard_cols;
-    p.ld = ld;
-    p.k_use = k_use;
-    p.mode = mxs::MODE_EMIT;
-    p.col_offset = col_offset;
-    p.out_cand = d_cand;
-    p.out_count = d_count;
-    p.out_flags = d_flags;
-    p.out_cap = cap;
-    d->clean_rows = -1;
-    fill_workspace(p, pl, d->ws, *d);
-    return launch(p, pl, (cudaStream_t)stream);
+    return mxs::shard_step(d_shard_logits, rows, shard_cols, ld, col_offset, top_k, cap, d_cand, d_count, d_flags,
+                           nullptr, stream, nullptr);
 }
 
 int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count_all, const uint32_t* d_flags_all,
@@ -458,10 +473,32 @@ int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count_all, co
     int rc = current_device(&d);
     if (rc) return rc;
     clamp_p(&top_p, &min_p);
+    Params p{};
+    if (k_use <= mxs::KSPLIT) {
+        // one warp per row (no workspace)
+        p.rows = rows;
+        p.vocab = vocab;
+        p.temperature = temperature;
+        p.top_p = top_p;
+        p.min_p = min_p;
+        p.k_use = k_use;
+        p.u = d_u;
+        p.next = d_next;
+        p.topk_idx = d_topk_idx;
+        p.topk_prob = d_topk_prob;
+        p.row_flags = d_row_flags;
+        p.status = d->status;
+        p.mode = mxs::MODE_MERGE;
+        p.in_cand = d_cand_all;
+        p.in_count = d_count_all;
+        p.in_flags = d_flags_all;
+        p.nshards = nshards;
+        p.in_cap = cap;
+        return mxs::merge_rows_launch(p, (cudaStream_t)stream) == cudaSuccess ? MXS_OK : MXS_ERR_CUDA;
+    }
     const Plan pl = make_plan(*d, rows, vocab, k_use, true);
     rc = ensure_library_ws(*d, pl.total, (cudaStream_t)stream);
     if (rc) return rc;
-    Params p{};
     p.rows = rows;
     p.vocab = vocab;
     p.ld = vocab;

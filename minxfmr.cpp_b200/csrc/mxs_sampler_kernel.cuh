@@ -66,6 +66,7 @@ struct Params {
     uint32_t* out_count;   // MODE_EMIT: rows
     uint32_t* out_flags;   // MODE_EMIT: rows
     int out_cap;
+    uint32_t* log_count;   // MODE_EMIT on the two-kernel path: rows, the streaming list's length (nullable)
     const uint64_t* in_cand;   // MODE_MERGE: nshards x rows x in_cap
     const uint32_t* in_count;  // MODE_MERGE: nshards x rows
     const uint32_t* in_flags;  // MODE_MERGE: nshards x rows (nullable)

@@ -902,32 +902,31 @@ __device__ unsigned long long g_fin_prof[8];
 #define MXS_FIN_ADD(i, x) (void)0
 #endif
 
-// Gather row `row`'s candidate list into w.keys / w.idx: taken in batches
-// against a running bound (the k-th largest key held once the buffer has
-// filled), so lists longer than the buffer (a row split over many chunks)
-// still fit. Returns the count; sets *massive when ties keep the buffer full.
-__device__ __forceinline__ int gather_row_list(const Params& p, int64_t row, FinishWarpSmem& w, uint32_t cnt_all,
-                                           int k, bool* massive) {
+// Gather the entries of src[0, n) whose key is >= `bound` into w.keys / w.idx
+// (after the cnt entries already there), raising the bound to the k-th largest
+// key held whenever the buffer fills, so lists longer than the buffer still
+// fit. Sets massive when ties keep the buffer full. seg_min (nullable) gets the
+// smallest key of the segment.
+__device__ __forceinline__ void gather_segment(const uint64_t* src, int n, FinishWarpSmem& w, int k, int& cnt,
+                                               uint32_t& bound, bool& massive, uint32_t* seg_min = nullptr) {
     const int lane = threadIdx.x & 31;
-    bool exact = false;
-    const uint64_t* src = p.row_cand + row * (int64_t)p.row_cap;
     const uint32_t lt = (1u << lane) - 1u;
-    int cnt = 0;
-    uint32_t bound = p.row_bound[row];  // the streaming warps' lower bound of the k-th largest
+    uint32_t mn = 0xFFFFFFFFu;
     // 256 entries per load round trip (8 per lane in flight).
-    for (int i0 = 0; i0 < (int)cnt_all && !exact; i0 += 256) {
+    for (int i0 = 0; i0 < n && !massive; i0 += 256) {
         uint64_t vv[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int i = i0 + 32 * j + lane;
-            vv[j] = i < (int)cnt_all ? src[i] : 0ull;
+            vv[j] = i < n ? src[i] : 0ull;
+            if (i < n) mn = min(mn, (uint32_t)(vv[j] >> 32));
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            if (exact || i0 + 32 * j >= (int)cnt_all) break;
+            if (massive || i0 + 32 * j >= n) break;
             const int i = i0 + 32 * j + lane;
             const uint64_t v = vv[j];
-            const bool take = i < (int)cnt_all && (uint32_t)(v >> 32) >= bound;
+            const bool take = i < n && (uint32_t)(v >> 32) >= bound;
             const uint32_t bal = __ballot_sync(0xffffffffu, take);
             if (take) {
                 const int pos = cnt + __popc(bal & lt);
@@ -937,51 +936,134 @@ __device__ __forceinline__ int gather_row_list(const Params& p, int64_t row, Fin
             cnt += __popc(bal);
             __syncwarp();
             if (cnt > FCAP - 32) {
-                MXS_FIN_ADD(7, 1);
                 bound = warp_select_kth_small(w.keys, cnt, k);
                 cnt = warp_compact_ge(w.keys, w.idx, cnt, bound);
-                if (cnt > FCAP - 32) exact = true;  // massive ties
+                if (cnt > FCAP - 32) massive = true;  // massive ties
             }
         }
     }
-    *massive = exact;
+    if (seg_min) *seg_min = __reduce_min_sync(0xffffffffu, mn);
+}
+
+// Row `row`'s candidate list into w.keys / w.idx, starting from the streaming
+// warps' lower bound of the row's k-th largest. Returns the count; sets
+// *massive when ties keep the buffer full.
+__device__ __forceinline__ int gather_row_list(const Params& p, int64_t row, FinishWarpSmem& w, uint32_t cnt_all,
+                                           int k, bool* massive) {
+    int cnt = 0;
+    uint32_t bound = p.row_bound[row];
+    bool m = false;
+    gather_segment(p.row_cand + row * (int64_t)p.row_cap, (int)cnt_all, w, k, cnt, bound, m);
+    *massive = m;
     return cnt;
 }
 
 // MODE_EMIT (vocab-sharded step 1 on this path): publish row `row`'s candidate
-// list - every logit of the shard >= the shard's k-th largest value - with
-// global column indices, as the CTA kernels' emit_list does. A row the list
-// cannot represent (NaN, overflow, massive ties) gets a count of 0 and a flag,
-// and the merge hands it back.
+// list -- every logit of the shard >= the shard's k-th largest value -- with
+// global column indices: first every logit above the k-th largest (fewer than
+// k), then those equal to it. When more tie at the k-th largest than out_cap
+// holds, the list keeps as many as fit and gets FLAG_EXACT ("truncated": every
+// logit left out equals the list's smallest value). A row the list cannot
+// represent (NaN, overflow, massive ties) gets a count of 0 and a flag, and
+// the merge hands it back. The row's streaming-list length is kept in
+// log_count (when given) for a later replay; the list itself stays in the
+// workspace until the next call.
 __device__ void emit_row_warp(const Params& p, int64_t row, FinishWarpSmem& w) {
     const int lane = threadIdx.x & 31;
+    const uint32_t lt = (1u << lane) - 1u;
     const int k = p.k_use;
     uint32_t flags = p.row_flag[row] & (FLAG_NAN | FLAG_OVERFLOW | FLAG_TIMEOUT);
     const uint32_t cnt_all = p.row_cnt[row];
     if (!flags && (cnt_all > (uint32_t)p.row_cap || cnt_all < (uint32_t)k)) flags |= FLAG_OVERFLOW;
-    int cnt = 0;
+    int n_out = 0;
+    uint64_t* dst = p.out_cand + row * p.out_cap;
     if (!flags) {
         bool massive = false;
-        cnt = gather_row_list(p, row, w, cnt_all, k, &massive);
-        if (massive) flags |= FLAG_OVERFLOW;
-        if (!flags && cnt > k) {
+        int cnt = gather_row_list(p, row, w, cnt_all, k, &massive);
+        if (massive) {
+            flags |= FLAG_OVERFLOW;
+        } else {
             const uint32_t kth = warp_select_kth_small(w.keys, cnt, k);
             cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
+            int pos = 0;
+            for (int pass = 0; pass < 2; ++pass) {  // above the k-th largest, then equal to it
+                for (int i0 = 0; i0 < cnt; i0 += 32) {
+                    const int i = i0 + lane;
+                    const bool take = i < cnt && (pass == 0 ? w.keys[i] > kth : w.keys[i] == kth);
+                    const uint32_t bal = __ballot_sync(0xffffffffu, take);
+                    const int at = pos + __popc(bal & lt);
+                    if (take && at < p.out_cap)
+                        dst[at] = ((uint64_t)w.keys[i] << 32) | (uint32_t)(w.idx[i] + (int32_t)p.col_offset);
+                    pos += __popc(bal);
+                }
+            }
+            n_out = min(pos, p.out_cap);
+            if (pos > p.out_cap) flags |= FLAG_EXACT;
         }
-        if (cnt > p.out_cap) flags |= FLAG_OVERFLOW;
-        if (flags) cnt = 0;
     }
-    uint64_t* dst = p.out_cand + row * p.out_cap;
-    for (int i = lane; i < cnt; i += 32)
-        dst[i] = ((uint64_t)w.keys[i] << 32) | (uint32_t)(w.idx[i] + (int32_t)p.col_offset);
     if (lane == 0) {
-        p.out_count[row] = (uint32_t)cnt;
+        p.out_count[row] = (uint32_t)n_out;
         p.out_flags[row] = flags;
+        if (p.log_count) p.log_count[row] = cnt_all;
         if (flags & FLAG_TIMEOUT) atomicOr(p.status, flags);
         p.row_cnt[row] = 0u;  // left clear for the next call on this workspace
         p.row_flag[row] = 0u;
         p.row_bound[row] = 0u;
     }
+}
+
+// MODE_MERGE on this path (k <= KSPLIT_K): one warp merges row `row`'s shard
+// lists (nshards blocks of [rows x in_cap] words), selects the k largest,
+// checks for ties and draws. Handed back (next = -1, MXS_ROW_EXACT plus the
+// shard flags) are rows with a flagged shard list (NaN, overflow, timeout), a
+// truncated list whose left-out logits could be among the k largest, and tie
+// rows whose order matters (a requested top-k list, or a draw that lands on a
+// tied position): their tie order depends on logits no list holds.
+__device__ void merge_row_warp(const Params& p, int64_t row, FinishWarpSmem& w) {
+    const int lane = threadIdx.x & 31;
+    const int k = p.k_use;
+    uint32_t bad = 0u, trunc_min = 0u;
+    int cnt = 0;
+    uint32_t bound = 0u;
+    bool massive = false;
+    for (int s = 0; s < p.nshards; ++s) {
+        const int64_t at = (int64_t)s * p.rows + row;
+        const uint32_t fl = p.in_flags ? p.in_flags[at] : 0u;
+        if (fl & (FLAG_NAN | FLAG_OVERFLOW | FLAG_TIMEOUT)) {
+            bad |= fl & (FLAG_NAN | FLAG_OVERFLOW | FLAG_TIMEOUT);
+            continue;
+        }
+        const int n = (int)min(p.in_count[at], (uint32_t)p.in_cap);
+        uint32_t mn = 0u;
+        gather_segment(p.in_cand + at * p.in_cap, n, w, k, cnt, bound, massive, &mn);
+        if ((fl & FLAG_EXACT) && n > 0) trunc_min = max(trunc_min, mn);
+    }
+    bool back = bad != 0u || massive || cnt < k;
+    if (!back) {
+        bool tie = false;
+        if (cnt > k) {
+            const uint32_t kth = warp_select_kth_small(w.keys, cnt, k);
+            cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
+            tie = cnt != k;
+            back = trunc_min >= kth;  // left-out logits would be among the k largest
+        } else {
+            back = trunc_min >= warp_select_kth_small(w.keys, cnt, k);
+        }
+        if (!back && cnt > KSPLIT_K) back = true;
+        if (!back) back = (cnt <= 64) ? finish_sorted<2>(p, row, w, cnt, k, tie, lane)
+                                      : finish_sorted<4>(p, row, w, cnt, k, tie, lane);
+    }
+    if (lane == 0) {
+        if (back) p.next[row] = -1;
+        if (p.row_flags) p.row_flags[row] = back ? (FLAG_EXACT | bad) : 0u;
+    }
+}
+
+__global__ void __launch_bounds__(F_WARPS * 32) merge_rows_kernel(Params p) {
+    extern __shared__ __align__(128) unsigned char msmem[];
+    FinishWarpSmem& w = reinterpret_cast<FinishWarpSmem*>(msmem)[threadIdx.x >> 5];
+    const int64_t row = (int64_t)blockIdx.x * F_WARPS + (threadIdx.x >> 5);
+    if (row < p.rows) merge_row_warp(p, row, w);
 }
 
 __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w, uint32_t* out_flags,
@@ -1133,13 +1215,221 @@ __global__ void __launch_bounds__(F_WARPS * 32) emit_rows_kernel(Params p) {
     if (row < p.rows) emit_row_warp(p, row, ws[warp]);
 }
 
+// ---------------------------------------------------------------------------
+// Vocab-sharded tie rows. The reference's tie order is the heap process over
+// the whole row in column order. Shard 0 holds the row's first columns, so
+// rank 0 can run that process over its shard alone (first tiles reread, the
+// rest from its streaming lists) and hand on the heap it leaves. A later shard
+// s only has to supply, in column order, every logit that could still enter:
+// those strictly above the k-th largest logit before them, which is at least
+// the k-th largest of any earlier shard (that shard alone holds k logits at or
+// above it); the shard lists of the first pass give those values.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(F_WARPS * 32) vocab_replay_emit_kernel(VocabReplayArgs a) {
+    extern __shared__ __align__(128) unsigned char vsmem[];
+    FinishWarpSmem& w = reinterpret_cast<FinishWarpSmem*>(vsmem)[threadIdx.x >> 5];
+    const int lane = threadIdx.x & 31;
+    const uint32_t lt = (1u << lane) - 1u;
+    const int64_t i = (int64_t)blockIdx.x * F_WARPS + (threadIdx.x >> 5);
+    if (i >= a.n) return;
+    const int64_t r = a.list[i];
+    const int k = a.k;
+    const uint32_t bad_bits = FLAG_NAN | FLAG_OVERFLOW | FLAG_TIMEOUT;
+    uint32_t flags = 0u;
+    uint32_t lc = 0u;
+    if (!a.log || (a.p1_flags[(int64_t)a.rank * a.rows + r] & bad_bits)) {
+        flags = FLAG_OVERFLOW;
+    } else {
+        lc = a.log_count[r];
+        if (lc > (uint32_t)a.log_cap || lc < (uint32_t)k) flags = FLAG_OVERFLOW;
+    }
+    const float* x = a.shard + r * a.ld;
+    const uint64_t* log = flags ? nullptr : a.log + r * (int64_t)a.log_cap;
+    uint64_t* dst = a.out + i * (int64_t)a.cap2;
+    const int64_t C = a.cols;
+    const int64_t chunk = (int64_t)a.tpc * S_TILE;
+    int n_out = 0;
+    if (!flags && a.rank == 0) {
+        const SoaHeap h{w.hv, w.hi};
+        Ent* slot = reinterpret_cast<Ent*>(w.keys);
+        for (int j = lane; j < k; j += 32) {
+            w.hv[j + 1] = x[j];
+            w.hi[j + 1] = j;
+        }
+        __syncwarp();
+        if (lane == 0) soa_build(h, k);
+        __syncwarp();
+        float r0 = w.hv[1];
+        for (int c = 0; c < a.S; ++c) {
+            const int64_t c0 = c * chunk;
+            if (c0 >= C) break;
+            const int64_t t1 = min(C, c0 + S_TILE), ce = min(C, c0 + chunk);
+            r0 = warp_replay_range(x, C, max(c0, (int64_t)k), t1, h, k, slot, r0);
+            __syncwarp();
+            r0 = warp_replay_list(log, (int)lc, t1, ce, h, k, slot, r0);
+            __syncwarp();
+        }
+        for (int j = lane; j < k; j += 32)
+            dst[j] = ((uint64_t)fkey(w.hv[j + 1]) << 32) | (uint32_t)(w.hi[j + 1] + (int32_t)a.col_offset);
+        n_out = k;
+    } else if (!flags) {
+        uint32_t B = 0u;  // largest k-th largest key of the earlier shards
+        for (int s2 = 0; s2 < a.rank && !flags; ++s2) {
+            const int64_t at = (int64_t)s2 * a.rows + r;
+            if (a.p1_flags[at] & bad_bits) {
+                flags = FLAG_OVERFLOW;
+                break;
+            }
+            const int n = (int)min(a.p1_count[at], (uint32_t)a.p1_cap);
+            const uint64_t* src = a.p1_cand + at * a.p1_cap;
+            uint32_t mn = 0xFFFFFFFFu;
+            for (int j = lane; j < n; j += 32) mn = min(mn, (uint32_t)(src[j] >> 32));
+            mn = __reduce_min_sync(0xffffffffu, mn);
+            if (n > 0) B = max(B, mn);
+        }
+        int cnt = 0;
+        auto put = [&](bool take, uint32_t key, int32_t col) {
+            const uint32_t bal = __ballot_sync(0xffffffffu, take);
+            const int at = cnt + __popc(bal & lt);
+            if (take && at < FCAP) {
+                w.keys[at] = key;
+                w.idx[at] = col;
+            }
+            cnt += __popc(bal);
+        };
+        for (int c = 0; c < a.S && !flags; ++c) {
+            const int64_t c0 = c * chunk;
+            if (c0 >= C) break;
+            const int64_t t1 = min(C, c0 + S_TILE), ce = min(C, c0 + chunk);
+            // the chunk's first tile from memory, the later tiles from the list
+            for (int64_t g = c0; g < t1; g += 128) {
+                const int64_t j = g + 4 * lane;
+                float4 v{0.f, 0.f, 0.f, 0.f};
+                if (j < t1) xload4(x, j, C, v);
+                const float e4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const bool in = j + t < t1;
+                    const uint32_t key = in ? fkey(e4[t]) : 0u;
+                    put(in && key > B && !(e4[t] != e4[t]), key, (int32_t)(j + t));
+                }
+            }
+            for (int j0 = 0; j0 < (int)lc; j0 += 32) {
+                const int j = j0 + lane;
+                const uint64_t v = j < (int)lc ? log[j] : 0ull;
+                const int64_t col = (int64_t)(uint32_t)v;
+                put(j < (int)lc && col >= t1 && col < ce && (uint32_t)(v >> 32) > B, (uint32_t)(v >> 32),
+                    (int32_t)col);
+            }
+            __syncwarp();
+        }
+        if (cnt > a.cap2 || cnt > FCAP) {
+            flags = FLAG_OVERFLOW;
+        } else {
+            // column order: keys (~column << 32 | value key) sorted descending
+            constexpr int NS = FCAP / 32;
+            uint64_t b[NS];
+#pragma unroll
+            for (int q = 0; q < NS; ++q) {
+                const int j = lane + 32 * q;
+                b[q] = j < cnt ? ((uint64_t)(~(uint32_t)w.idx[j]) << 32) | w.keys[j] : 0ull;
+            }
+            warp_sort_desc<NS>(b);
+#pragma unroll
+            for (int q = 0; q < NS; ++q) {
+                const int j = lane + 32 * q;
+                if (j < cnt)
+                    dst[j] = ((uint64_t)(uint32_t)b[q] << 32) |
+                             (uint32_t)((int32_t)~(uint32_t)(b[q] >> 32) + (int32_t)a.col_offset);
+            }
+            n_out = cnt;
+        }
+    }
+    if (lane == 0) {
+        a.out_count[i] = flags ? 0u : (uint32_t)n_out;
+        a.out_flags[i] = flags;
+    }
+}
+
+__global__ void __launch_bounds__(F_WARPS * 32) vocab_replay_merge_kernel(VocabReplayArgs a, Params d) {
+    extern __shared__ __align__(128) unsigned char vsmem[];
+    FinishWarpSmem& w = reinterpret_cast<FinishWarpSmem*>(vsmem)[threadIdx.x >> 5];
+    const int lane = threadIdx.x & 31;
+    const int64_t i = (int64_t)blockIdx.x * F_WARPS + (threadIdx.x >> 5);
+    if (i >= a.n) return;
+    const int64_t r = a.list[i];
+    const int k = a.k;
+    uint32_t bad = 0u;
+    for (int s2 = 0; s2 < a.world; ++s2) bad |= a.g_flags[(int64_t)s2 * a.n + i];
+    if (bad || a.g_count[i] != (uint32_t)k) {
+        if (lane == 0) a.need_full[i] = 1u;
+        return;
+    }
+    const SoaHeap h{w.hv, w.hi};
+    Ent* slot = reinterpret_cast<Ent*>(w.keys);
+    const uint64_t* h0 = a.g_cand + i * (int64_t)a.cap2;  // rank 0's heap, heap order
+    for (int j = lane; j < k; j += 32) {
+        const uint64_t v = h0[j];
+        w.hv[j + 1] = fkey_inv((uint32_t)(v >> 32));
+        w.hi[j + 1] = (int32_t)(uint32_t)v;
+    }
+    __syncwarp();
+    float r0 = w.hv[1];
+    for (int s2 = 1; s2 < a.world; ++s2) {
+        const int64_t at = (int64_t)s2 * a.n + i;
+        const int n = (int)min(a.g_count[at], (uint32_t)a.cap2);
+        const uint64_t* src = a.g_cand + at * a.cap2;
+        for (int j0 = 0; j0 < n; j0 += XSLOT) {
+            const int m = min(XSLOT, n - j0);
+            for (int j = lane; j < m; j += 32) {
+                const uint64_t v = src[j0 + j];
+                slot[j] = Ent{fkey_inv((uint32_t)(v >> 32)), (int32_t)(uint32_t)v};
+            }
+            __syncwarp();
+            if (lane == 0) r0 = soa_offer_list(h, k, slot, m, r0);
+            r0 = __shfl_sync(0xffffffffu, r0, 0);
+        }
+    }
+    if (lane == 0) soa_sort(h, k);
+    __syncwarp();
+    for (int j = lane; j < k; j += 32) w.e[j] = Ent{w.hv[j + 1], w.hi[j + 1]};
+    __syncwarp();
+    warp_draw(d, r, w.e, k, w.pbuf);
+    if (lane == 0) a.need_full[i] = 0u;
+}
+
+cudaError_t vocab_replay_emit_launch(const VocabReplayArgs& a, cudaStream_t stream) {
+    if (a.n == 0) return cudaSuccess;
+    vocab_replay_emit_kernel<<<(unsigned)((a.n + F_WARPS - 1) / F_WARPS), F_WARPS * 32,
+                               sizeof(FinishWarpSmem) * F_WARPS, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t vocab_replay_merge_launch(const VocabReplayArgs& a, const Params& draw, cudaStream_t stream) {
+    if (a.n == 0) return cudaSuccess;
+    vocab_replay_merge_kernel<<<(unsigned)((a.n + F_WARPS - 1) / F_WARPS), F_WARPS * 32,
+                                sizeof(FinishWarpSmem) * F_WARPS, stream>>>(a, draw);
+    return cudaGetLastError();
+}
+
 size_t stream_smem_bytes() { return S_SMEM; }
+
+cudaError_t merge_rows_launch(const Params& p, cudaStream_t stream) {
+    merge_rows_kernel<<<(unsigned)((p.rows + F_WARPS - 1) / F_WARPS), F_WARPS * 32, sizeof(FinishWarpSmem) * F_WARPS,
+                        stream>>>(p);
+    return cudaGetLastError();
+}
 
 cudaError_t stream_path_configure(int* blocks_per_sm) {
     cudaError_t e = cudaFuncSetAttribute(stream_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(finish_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F_SMEM);
     if (e != cudaSuccess) return e;
+    for (const void* f : {(const void*)merge_rows_kernel, (const void*)vocab_replay_emit_kernel,
+                          (const void*)vocab_replay_merge_kernel}) {
+        e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sizeof(FinishWarpSmem) * F_WARPS));
+        if (e != cudaSuccess) return e;
+    }
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, stream_select_kernel, NT_WS, S_SMEM);
 }
 

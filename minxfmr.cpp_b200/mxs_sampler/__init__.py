@@ -38,7 +38,7 @@ EXPORTS = (
     "mxs_sample_topk", "mxs_sample_topk_ex", "mxs_workspace_size", "mxs_workspace_init",
     "mxs_sample_topk_host", "mxs_shard_candidates", "mxs_merge_sample", "mxs_get_status",
     "mxs_version", "mxs_sample_topk_noalloc", "mxs_set_profile_events", "mxs_sample_rowsharded",
-    "mxs_sample_vocabsharded", "mxs_set_test_hooks",
+    "mxs_sample_vocabsharded", "mxs_set_test_hooks", "mxs_vocabsharded_stats",
 )
 
 _P = ctypes.c_void_p
@@ -62,6 +62,7 @@ _SIGS = {
                               ctypes.POINTER(_I64), _P],
     "mxs_sample_vocabsharded": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _P, _P],
     "mxs_set_test_hooks": [_I64, _I, _I],
+    "mxs_vocabsharded_stats": [ctypes.POINTER(_I64), ctypes.POINTER(_I64)],
 }
 
 _lib = None
@@ -314,6 +315,14 @@ def sample_vocabsharded(shard_logits, temperature, top_k, u, comm, top_p=1.0, mi
                                             _stream(stream))
     _check("mxs_sample_vocabsharded", rc)
     return nxt, idx, prob, flg
+
+
+def vocabsharded_stats():
+    """(tie rows resolved from lists, rows gathered whole) of the last
+    sample_vocabsharded call on the current device."""
+    a, b = ctypes.c_int64(), ctypes.c_int64()
+    _check("mxs_vocabsharded_stats", load().mxs_vocabsharded_stats(ctypes.byref(a), ctypes.byref(b)))
+    return a.value, b.value
 
 
 def set_profile_events(start=None, stop=None):

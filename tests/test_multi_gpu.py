@@ -57,17 +57,20 @@ obj = [nccl.get_unique_id() if rank == 0 else None]
 dist.broadcast_object_list(obj, 0)
 comm = nccl.comm_init_rank(world, obj[0], rank)
 ok_abi = True
-for xx in (x, torch.from_numpy(workloads.normal(78, 48, V, 2.0)).bfloat16().float().numpy()):
+whole = []
+bf16 = torch.from_numpy(workloads.normal(78, 48, V, 2.0)).bfloat16().float().numpy()
+for xx, kk in ((x, k), (bf16, k), (bf16, 8), (bf16, 128)):
     uu = oracle_lib.uniforms(78, xx.shape[0])
     sh = torch.from_numpy(xx[:, rank * cols:(rank + 1) * cols].copy()).cuda()
-    n2, i2, p2, f2 = mxs_sampler.sample_vocabsharded(sh, T, k, torch.from_numpy(uu).cuda(), comm)
+    n2, i2, p2, f2 = mxs_sampler.sample_vocabsharded(sh, T, kk, torch.from_numpy(uu).cuda(), comm)
     torch.cuda.synchronize()
-    m0, j0, q0 = oracle_lib.oracle_sample(xx, T, k, uu)
+    whole.append(mxs_sampler.vocabsharded_stats()[1])
+    m0, j0, q0 = oracle_lib.oracle_sample(xx, T, kk, uu)
     ok_abi = ok_abi and bool((n2.cpu().numpy() == m0).all() and (i2.cpu().numpy() == j0).all()
                              and np.allclose(p2.cpu().numpy(), q0, rtol=1e-6, atol=0))
 nccl.comm_destroy(comm)
-print(json.dumps({"rank": rank, "ok": ok, "ok_abi": ok_abi, "exact_rows": int((fl.cpu().numpy() & 1).sum())}),
-      flush=True)
+print(json.dumps({"rank": rank, "ok": ok, "ok_abi": ok_abi, "exact_rows": int((fl.cpu().numpy() & 1).sum()),
+                  "rows_gathered_whole": whole}), flush=True)
 dist.destroy_process_group()
 sys.exit(0 if (ok and ok_abi) else 3)
 '''
@@ -93,6 +96,7 @@ def test_vocab_sharded_nccl(world):
         line = [l for l in o.splitlines() if l.startswith("{")][-1]
         d = json.loads(line)
         assert d["ok"] and d["ok_abi"]
+        assert d["rows_gathered_whole"] == [0, 0, 0, 0], d  # ties resolved from lists, bf16 rows included
 
 
 def test_bench_two_gpus_row_and_vocab_sharded():

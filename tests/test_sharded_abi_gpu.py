@@ -47,12 +47,24 @@ def test_vocabsharded_one_rank_normal_rows(mxs, comm1, k):
 
 
 def test_vocabsharded_one_rank_all_rows_tied(mxs, comm1):
-    """bf16-rounded logits: nearly every row takes the full-row pass, in more
-    than one chunk (600 rows > 512 per chunk)."""
+    """bf16-rounded logits: nearly every row ties; their ties are resolved from
+    lists, with no row gathered whole."""
     x = torch.from_numpy(workloads.normal(510, 600, 32768, 2.0)).bfloat16().float().numpy()
     u = oracle_lib.uniforms(510, 600)
     fl = _vocab_case(mxs, comm1, x, 1.0, 50, u, top_p=0.9)
     assert (fl & mxs.ROW_EXACT).mean() > 0.9
+    from_lists, whole = mxs.vocabsharded_stats()
+    assert whole == 0 and from_lists == int((fl & mxs.ROW_EXACT).sum())
+
+
+def test_vocabsharded_one_rank_large_k_takes_full_rows(mxs, comm1):
+    """top_k above 128: tie rows are gathered whole (in more than one chunk:
+    600 rows > 512 per chunk)."""
+    x = torch.from_numpy(workloads.normal(511, 600, 32768, 2.0)).bfloat16().float().numpy()
+    u = oracle_lib.uniforms(511, 600)
+    fl = _vocab_case(mxs, comm1, x, 1.0, 200, u)
+    from_lists, whole = mxs.vocabsharded_stats()
+    assert from_lists == 0 and whole == int((fl & mxs.ROW_EXACT).sum()) > 512
 
 
 def test_vocabsharded_special_rows(mxs, comm1):
