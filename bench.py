@@ -223,8 +223,11 @@ def vocab_measure(rows, steps, warmup, check_rows=64):
     comm = nccl.comm_init_rank(world, obj[0], rank)
     stream = torch.cuda.current_stream()
 
+    # Timed like the row-sharded line: the sampled ids only (a tie row then
+    # needs its heap replay only when the draw lands on a tied position); the
+    # parity check below also returns the top-k order and probabilities.
     def step(topk=False):
-        return mxs_sampler.sample_vocabsharded(shard, TEMPERATURE, TOP_K, u, comm, stream=stream)
+        return mxs_sampler.sample_vocabsharded(shard, TEMPERATURE, TOP_K, u, comm, stream=stream, return_topk=topk)
 
     for _ in range(warmup):
         step()
@@ -241,7 +244,7 @@ def vocab_measure(rows, steps, warmup, check_rows=64):
     ms = ev0.elapsed_time(ev1)
     per_rank = _gather_floats([ms / steps], dev, world)
     ms_step = max(r[0] for r in per_rank)
-    nxt, idx, prob, flg = step()
+    nxt, idx, prob, flg = step(topk=True)
     torch.cuda.synchronize()
     from_lists, whole = mxs_sampler.vocabsharded_stats()
     # bf16-rounded rows (a bf16 lm_head upcast): ties in nearly every row's top-k

@@ -187,64 +187,58 @@ __device__ __forceinline__ void heap_sort_top(Ent* h, int len) {
     }
 }
 
-// The same top-down heap for one thread, with values and indices in separate
-// 1-based arrays (node j of the 0-based heap is node j + 1 here), so the two
-// children of node i, 2i and 2i + 1, sit in one aligned 8-byte pair: each
-// level costs one dependent round trip for both values (and one, issued
-// alongside, for both indices). hv and hi need len + 2 entries and 8-byte
+// The same top-down heap for one thread, 1-based (node j of the 0-based heap
+// is node j + 1 here), so the two children of node i, 2i and 2i + 1, sit in one
+// aligned 16-byte pair: each level costs one dependent shared-memory load for
+// both children and one store. `h` needs len + 2 entries and 16-byte
 // alignment. Heaps without NaN only; the results equal heap_build /
-// heap_place_top1 / heap_sort_top on the Ent layout.
-struct SoaHeap {
-    float* v;    // v[1 .. len]
-    int32_t* i;  // i[1 .. len]
+// heap_place_top1 / heap_sort_top on the 0-based layout.
+struct PairHeap {
+    Ent* h;  // h[1 .. len]
 };
 
-// Place (ev, ei) at hole `hole` of the subtree below it, top-down; returns the
-// value left at `hole`.
-__device__ __forceinline__ float soa_place(SoaHeap h, int hole, int len, float ev, int32_t ei) {
+// Place e at hole `hole` of the subtree below it, top-down; returns the value
+// left at `hole`.
+__device__ __forceinline__ float pair_place(PairHeap hp, int hole, int len, Ent e) {
     const int top = hole;
-    float top_v = ev;
+    float top_v = e.v;
     for (;;) {
         const int c = 2 * hole;
         if (c > len) break;
-        const float2 cv = *reinterpret_cast<const float2*>(h.v + c);
-        const int2 ci = *reinterpret_cast<const int2*>(h.i + c);
-        const bool right = (c + 1 <= len) && !before(cv.y, cv.x);
-        const float chv = right ? cv.y : cv.x;
-        if (before(chv, ev)) break;
-        h.v[hole] = chv;
-        h.i[hole] = right ? ci.y : ci.x;
+        const int4 pr = *reinterpret_cast<const int4*>(hp.h + c);
+        const float lv = __int_as_float(pr.x), rv = __int_as_float(pr.z);
+        const bool right = (c + 1 <= len) && !before(rv, lv);
+        const float chv = right ? rv : lv;
+        if (before(chv, e.v)) break;
+        hp.h[hole] = Ent{chv, right ? pr.w : pr.y};
         if (hole == top) top_v = chv;
         hole = c + (right ? 1 : 0);
     }
-    h.v[hole] = ev;
-    h.i[hole] = ei;
+    hp.h[hole] = e;
     return top_v;
 }
 
 // Floyd's build over nodes 1..len (parents len/2 down to 1).
-__device__ __forceinline__ void soa_build(SoaHeap h, int len) {
-    for (int p = len / 2; p >= 1; --p) soa_place(h, p, len, h.v[p], h.i[p]);
+__device__ __forceinline__ void pair_build(PairHeap hp, int len) {
+    for (int p = len / 2; p >= 1; --p) pair_place(hp, p, len, hp.h[p]);
 }
 
 // Offers list[0, n) in order; returns the root value.
-__device__ __forceinline__ float soa_offer_list(SoaHeap h, int len, const Ent* list, int n, float root) {
+__device__ __forceinline__ float pair_offer_list(PairHeap hp, int len, const Ent* list, int n, float root) {
     for (int j = 0; j < n; ++j) {
         const Ent e = list[j];
-        if (before(e.v, root)) root = soa_place(h, 1, len, e.v, e.i);
+        if (before(e.v, root)) root = pair_place(hp, 1, len, e);
     }
     return root;
 }
 
 // sort_heap: afterwards nodes 1..len hold the reference's top-k order.
-__device__ __forceinline__ void soa_sort(SoaHeap h, int len) {
+__device__ __forceinline__ void pair_sort(PairHeap hp, int len) {
     while (len > 1) {
-        const float ev = h.v[len];
-        const int32_t ei = h.i[len];
-        h.v[len] = h.v[1];
-        h.i[len] = h.i[1];
+        const Ent e = hp.h[len];
+        hp.h[len] = hp.h[1];
         --len;
-        soa_place(h, 1, len, ev, ei);
+        pair_place(hp, 1, len, e);
     }
 }
 

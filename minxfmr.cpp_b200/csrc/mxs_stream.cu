@@ -504,9 +504,8 @@ struct FinishWarpSmem {
     int32_t idx[FCAP];
     double pbuf[KSPLIT_K];
     Ent e[KSPLIT_K];
-    // the replay's heap: values and indices, 1-based (soa_* in mxs_heap.cuh)
-    alignas(8) float hv[KSPLIT_K + 2];
-    alignas(8) int32_t hi[KSPLIT_K + 2];
+    // the replay's heap, 1-based (pair_* in mxs_heap.cuh)
+    alignas(16) Ent hp[KSPLIT_K + 2];
 };
 
 // Draws for row `row` from e[0, k) and writes next (and the optional outputs);
@@ -646,7 +645,7 @@ extern "C" __attribute__((visibility("default"))) int mxs_prof_read_rep(unsigned
 // another quarter step. The root only rises (no NaN), so a stale root lets
 // through a superset of the logits that enter, and each offer makes the exact
 // comparison itself. Returns the root (in every lane).
-__device__ __noinline__ float warp_replay_range(const float* x, int64_t V, int64_t lo, int64_t hi, SoaHeap h,
+__device__ __noinline__ float warp_replay_range(const float* x, int64_t V, int64_t lo, int64_t hi, PairHeap h,
                                                 int k, Ent* slot, float r0) {
     const int lane = threadIdx.x & 31;
     if (lo >= hi) return r0;
@@ -672,7 +671,7 @@ __device__ __noinline__ float warp_replay_range(const float* x, int64_t V, int64
             if (c > XSLOT - 128) {
                 __syncwarp();
                 MXS_REP_T(o0);
-                if (lane == 0) r0 = soa_offer_list(h, k, slot, c, r0);
+                if (lane == 0) r0 = pair_offer_list(h, k, slot, c, r0);
                 MXS_REP_T(o1);
                 MXS_REP_ADD(6, o1 - o0);
                 MXS_REP_ADD(7, c);
@@ -696,7 +695,7 @@ __device__ __noinline__ float warp_replay_range(const float* x, int64_t V, int64
     }
     __syncwarp();
     MXS_REP_T(o0);
-    if (lane == 0) r0 = soa_offer_list(h, k, slot, c, r0);
+    if (lane == 0) r0 = pair_offer_list(h, k, slot, c, r0);
     MXS_REP_T(o1);
     MXS_REP_ADD(6, o1 - o0);
     MXS_REP_ADD(7, c);
@@ -707,7 +706,7 @@ __device__ __noinline__ float warp_replay_range(const float* x, int64_t V, int64
 // root, in column order: windows of at most LWIN entries (halved until they
 // fit), each gathered into `slot`, sorted by column in registers and offered.
 constexpr int LWIN = 128;
-__device__ __noinline__ float warp_replay_list(const uint64_t* list, int n, int64_t lo, int64_t hi, SoaHeap h,
+__device__ __noinline__ float warp_replay_list(const uint64_t* list, int n, int64_t lo, int64_t hi, PairHeap h,
                                                int k, Ent* slot, float r0) {
     const int lane = threadIdx.x & 31;
     const uint32_t lt = (1u << lane) - 1u;
@@ -754,7 +753,7 @@ __device__ __noinline__ float warp_replay_list(const uint64_t* list, int n, int6
                 if (i < c) slot[i] = Ent{__uint_as_float((uint32_t)b[q]), (int32_t)~(uint32_t)(b[q] >> 32)};
             }
             __syncwarp();
-            if (lane == 0) r0 = soa_offer_list(h, k, slot, c, r0);
+            if (lane == 0) r0 = pair_offer_list(h, k, slot, c, r0);
             r0 = __shfl_sync(0xffffffffu, r0, 0);
         }
         lo = whi;
@@ -764,7 +763,7 @@ __device__ __noinline__ float warp_replay_list(const uint64_t* list, int n, int6
 
 // One warp replays the reference's partial_sort heap process over row `row`
 // without reading the whole row again, and draws. Rows without NaN, k <=
-// KSPLIT_K, whose list did not overflow. The heap lives in w.hv / w.hi; w.keys
+// KSPLIT_K, whose list did not overflow. The heap lives in w.hp; w.keys
 // / w.idx hold the replay list. A row is streamed as S chunks of TPC tiles; in
 // each chunk the logits of the first tile are read again from memory, and
 // those of the later tiles come from the row's list, which holds every one of
@@ -778,20 +777,17 @@ __device__ void exact_row_warp_log(const Params& p, int64_t row, FinishWarpSmem&
     const int64_t V = p.vocab;
     const float* x = p.logits + row * p.ld;
     const uint64_t* list = p.row_cand + row * (int64_t)p.row_cap;
-    const SoaHeap h{w.hv, w.hi};
+    const PairHeap h{w.hp};
     Ent* slot = reinterpret_cast<Ent*>(w.keys);
     MXS_REP_T(q0);
-    for (int i = lane; i < k; i += 32) {
-        w.hv[i + 1] = x[i];
-        w.hi[i + 1] = i;
-    }
+    for (int i = lane; i < k; i += 32) w.hp[i + 1] = Ent{x[i], i};
     __syncwarp();
-    if (lane == 0) soa_build(h, k);
+    if (lane == 0) pair_build(h, k);
     __syncwarp();
     MXS_REP_T(q1);
     MXS_REP_ADD(0, 1);
     MXS_REP_ADD(1, q1 - q0);
-    float r0 = w.hv[1];
+    float r0 = w.hp[1].v;
     const int64_t chunk = (int64_t)p.tiles_per_chunk * S_TILE;
     for (int c = 0; c < p.S; ++c) {
         const int64_t c0 = c * chunk;
@@ -808,9 +804,9 @@ __device__ void exact_row_warp_log(const Params& p, int64_t row, FinishWarpSmem&
         MXS_REP_ADD(3, q4 - q3);
     }
     MXS_REP_T(q5);
-    if (lane == 0) soa_sort(h, k);
+    if (lane == 0) pair_sort(h, k);
     __syncwarp();
-    for (int i = lane; i < k; i += 32) w.e[i] = Ent{w.hv[i + 1], w.hi[i + 1]};
+    for (int i = lane; i < k; i += 32) w.e[i] = w.hp[i + 1];
     __syncwarp();
     MXS_REP_T(q6);
     warp_draw(p, row, w.e, k, w.pbuf);
@@ -980,7 +976,7 @@ __device__ void emit_row_warp(const Params& p, int64_t row, FinishWarpSmem& w) {
     if (!flags) {
         bool massive = false;
         int cnt = gather_row_list(p, row, w, cnt_all, k, &massive);
-        if (massive) {
+        if (massive || cnt < k) {
             flags |= FLAG_OVERFLOW;
         } else {
             const uint32_t kth = warp_select_kth_small(w.keys, cnt, k);
@@ -1066,8 +1062,10 @@ __global__ void __launch_bounds__(F_WARPS * 32) merge_rows_kernel(Params p) {
     if (row < p.rows) merge_row_warp(p, row, w);
 }
 
+// *out_full: the row's list cannot stand for it (NaN, overflow, fewer than k
+// candidates), so a replay must read the whole row.
 __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w, uint32_t* out_flags,
-                                uint32_t* out_cnt) {
+                                uint32_t* out_cnt, bool* out_full) {
     const int lane = threadIdx.x & 31;
     MXS_FIN_T(f0);
     const int k = p.k_use;
@@ -1075,6 +1073,7 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
     const uint32_t cnt_all = p.row_cnt[row];
     bool exact = (flags & (FLAG_NAN | FLAG_OVERFLOW)) != 0 || cnt_all > (uint32_t)p.row_cap ||
                  cnt_all < (uint32_t)k;
+    bool full = exact;
     if (!(flags & FLAG_TIMEOUT) && !exact) {
         bool massive = false;
         int cnt = gather_row_list(p, row, w, cnt_all, k, &massive);
@@ -1097,6 +1096,7 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
             }
         } else if (!exact && cnt < k) {
             exact = true;
+            full = true;
         }
         MXS_FIN_T(f2);
         MXS_FIN_ADD(1, f2 - f1);
@@ -1121,6 +1121,7 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
     }
     *out_flags = flags;
     *out_cnt = cnt_all;
+    *out_full = full;
     return exact && !(flags & FLAG_TIMEOUT);
 }
 
@@ -1157,12 +1158,11 @@ __global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) 
     MXS_PROF_BEGIN();
     csync();
     uint32_t flags = 0u, cnt_all = 0u;
-    const bool need = row < p.rows && finish_row_warp(p, row, w, &flags, &cnt_all);
+    bool full = false;
+    const bool need = row < p.rows && finish_row_warp(p, row, w, &flags, &cnt_all, &full);
     // A row whose list stands for it (no NaN, no overflow, at least k entries)
     // is replayed by its own warp from the list and its chunks' first tiles;
     // the others read the whole row with the CTA.
-    const bool full = (flags & (FLAG_NAN | FLAG_OVERFLOW)) != 0 || cnt_all > (uint32_t)p.row_cap ||
-                      cnt_all < (uint32_t)p.k_use;
     if (lane == 0 && need && !full) atomicAdd(&s_wn, 1);
     csync();
     const bool by_warp = s_wn >= p.replay_warp_min;
@@ -1250,16 +1250,13 @@ __global__ void __launch_bounds__(F_WARPS * 32) vocab_replay_emit_kernel(VocabRe
     const int64_t chunk = (int64_t)a.tpc * S_TILE;
     int n_out = 0;
     if (!flags && a.rank == 0) {
-        const SoaHeap h{w.hv, w.hi};
+        const PairHeap h{w.hp};
         Ent* slot = reinterpret_cast<Ent*>(w.keys);
-        for (int j = lane; j < k; j += 32) {
-            w.hv[j + 1] = x[j];
-            w.hi[j + 1] = j;
-        }
+        for (int j = lane; j < k; j += 32) w.hp[j + 1] = Ent{x[j], j};
         __syncwarp();
-        if (lane == 0) soa_build(h, k);
+        if (lane == 0) pair_build(h, k);
         __syncwarp();
-        float r0 = w.hv[1];
+        float r0 = w.hp[1].v;
         for (int c = 0; c < a.S; ++c) {
             const int64_t c0 = c * chunk;
             if (c0 >= C) break;
@@ -1270,7 +1267,7 @@ __global__ void __launch_bounds__(F_WARPS * 32) vocab_replay_emit_kernel(VocabRe
             __syncwarp();
         }
         for (int j = lane; j < k; j += 32)
-            dst[j] = ((uint64_t)fkey(w.hv[j + 1]) << 32) | (uint32_t)(w.hi[j + 1] + (int32_t)a.col_offset);
+            dst[j] = ((uint64_t)fkey(w.hp[j + 1].v) << 32) | (uint32_t)(w.hp[j + 1].i + (int32_t)a.col_offset);
         n_out = k;
     } else if (!flags) {
         uint32_t B = 0u;  // largest k-th largest key of the earlier shards
@@ -1365,16 +1362,15 @@ __global__ void __launch_bounds__(F_WARPS * 32) vocab_replay_merge_kernel(VocabR
         if (lane == 0) a.need_full[i] = 1u;
         return;
     }
-    const SoaHeap h{w.hv, w.hi};
+    const PairHeap h{w.hp};
     Ent* slot = reinterpret_cast<Ent*>(w.keys);
     const uint64_t* h0 = a.g_cand + i * (int64_t)a.cap2;  // rank 0's heap, heap order
     for (int j = lane; j < k; j += 32) {
         const uint64_t v = h0[j];
-        w.hv[j + 1] = fkey_inv((uint32_t)(v >> 32));
-        w.hi[j + 1] = (int32_t)(uint32_t)v;
+        w.hp[j + 1] = Ent{fkey_inv((uint32_t)(v >> 32)), (int32_t)(uint32_t)v};
     }
     __syncwarp();
-    float r0 = w.hv[1];
+    float r0 = w.hp[1].v;
     for (int s2 = 1; s2 < a.world; ++s2) {
         const int64_t at = (int64_t)s2 * a.n + i;
         const int n = (int)min(a.g_count[at], (uint32_t)a.cap2);
@@ -1386,13 +1382,13 @@ __global__ void __launch_bounds__(F_WARPS * 32) vocab_replay_merge_kernel(VocabR
                 slot[j] = Ent{fkey_inv((uint32_t)(v >> 32)), (int32_t)(uint32_t)v};
             }
             __syncwarp();
-            if (lane == 0) r0 = soa_offer_list(h, k, slot, m, r0);
+            if (lane == 0) r0 = pair_offer_list(h, k, slot, m, r0);
             r0 = __shfl_sync(0xffffffffu, r0, 0);
         }
     }
-    if (lane == 0) soa_sort(h, k);
+    if (lane == 0) pair_sort(h, k);
     __syncwarp();
-    for (int j = lane; j < k; j += 32) w.e[j] = Ent{w.hv[j + 1], w.hi[j + 1]};
+    for (int j = lane; j < k; j += 32) w.e[j] = w.hp[j + 1];
     __syncwarp();
     warp_draw(d, r, w.e, k, w.pbuf);
     if (lane == 0) a.need_full[i] = 0u;

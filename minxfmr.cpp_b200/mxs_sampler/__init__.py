@@ -291,12 +291,13 @@ def sample_rowsharded(local_logits, global_rows, rank, world, temperature, top_k
     return nxt, idx, prob, flg
 
 
-def sample_vocabsharded(shard_logits, temperature, top_k, u, comm, top_p=1.0, min_p=0.0, stream=None):
+def sample_vocabsharded(shard_logits, temperature, top_k, u, comm, top_p=1.0, min_p=0.0, stream=None,
+                        return_topk=True):
     """One collective call per rank over an NCCL communicator (an integer
     ncclComm_t, e.g. from mxs_sampler.nccl.comm_init_rank): shard_logits is this
     rank's [rows, vocab / world] column shard, u the [rows] uniforms (the same on
     every rank). Returns (next, topk_idx, topk_prob, row_flags) for every row,
-    the same on every rank."""
+    the same on every rank (topk_idx / topk_prob None without return_topk)."""
     _need_cuda(shard_logits, "shard_logits", torch.float32)
     _need_cuda(u, "u", torch.float64)
     rows, cols = shard_logits.shape
@@ -305,8 +306,8 @@ def sample_vocabsharded(shard_logits, temperature, top_k, u, comm, top_p=1.0, mi
     dev = shard_logits.device
     k = k_use(int(top_k), vocab)
     nxt = torch.empty(rows, dtype=torch.int32, device=dev)
-    idx = torch.empty((rows, k), dtype=torch.int32, device=dev)
-    prob = torch.empty((rows, k), dtype=torch.float64, device=dev)
+    idx = torch.empty((rows, k), dtype=torch.int32, device=dev) if return_topk else None
+    prob = torch.empty((rows, k), dtype=torch.float64, device=dev) if return_topk else None
     flg = torch.empty(rows, dtype=torch.int32, device=dev)
     with torch.cuda.device(dev):
         rc = load().mxs_sample_vocabsharded(_ptr(shard_logits), rows, cols, shard_logits.stride(0),
