@@ -34,9 +34,9 @@ METRIC = "sampled rows/s (V=151936 fp32, top_k 50)"
 UNIT = "rows/s"
 # ncu dram__bytes_read.sum + dram__bytes_write.sum of one stream_select_kernel
 # launch per row of this workload, from an ncu capture of a 512-row launch of the
-# same kernel: 311,272,960 + 4,212,480 bytes / 512 rows. Traffic grows in
+# same kernel: 311,243,520 + 5,244,928 bytes / 512 rows. Traffic grows in
 # proportion to the rows, so it is scaled to a full launch.
-NCU_TRAFFIC_BYTES_PER_ROW = (311272960 + 4212480) / 512
+NCU_TRAFFIC_BYTES_PER_ROW = (311243520 + 5244928) / 512
 DOMINANT_KERNEL = "mxs::stream_select_kernel"
 
 
