@@ -102,7 +102,9 @@ MXS_API int mxs_workspace_init(void* d_workspace, size_t workspace_bytes, void* 
  * cuda_backend.cu:1440-1442, and samples there). Copies logits and u to the
  * device, samples, copies next (and the optional top-k outputs) back, and
  * returns when they are in host memory. Pinned host buffers make the copies
- * asynchronous DMA; pageable ones work too.
+ * asynchronous DMA; pageable ones work too. The device-side copies are reused
+ * from call to call, so calls on one device run one at a time (a per-device
+ * lock), as the reference's single-threaded generate loop does.
  */
 MXS_API int mxs_sample_topk_host(const float* h_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
                          int top_k, double top_p, double min_p, const double* h_u, int32_t* h_next,

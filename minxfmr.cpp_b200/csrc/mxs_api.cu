@@ -47,6 +47,7 @@ struct Device {
     size_t clean_off = 0;
     size_t ws_bytes = 0;
     HostBuffers hb;
+    std::mutex hb_mu;  // held for a whole host-buffer call: its buffers are reused by the next
 };
 
 std::mutex g_mu;
@@ -401,11 +402,16 @@ int mxs_sample_topk_host(const float* h_logits, int64_t rows, int64_t vocab, int
     cudaStream_t st = (cudaStream_t)stream;
     const int k_use = clamp_k(top_k, vocab);
     HostBuffers* hb;
+    Device* d;
     {
         std::lock_guard<std::mutex> lk(g_mu);
-        Device* d;
         int rc = current_device(&d);
         if (rc) return rc;
+    }
+    // One host-buffer call per device at a time: the device-side copies of the
+    // logits and outputs are reused by every call on the device.
+    std::lock_guard<std::mutex> hlk(d->hb_mu);
+    {
         hb = &d->hb;
         const size_t lb = sizeof(float) * (size_t)rows * vocab;
         const size_t tk = (size_t)rows * k_use;

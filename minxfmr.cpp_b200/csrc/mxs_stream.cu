@@ -17,6 +17,27 @@
 #include <cuda_runtime.h>
 
 #ifdef MXS_PROFILE
+// Phase clocks of the streaming kernel's consumer warp 0 (profiling build),
+// summed over CTAs: units, full-barrier waits, first-tile work, later-tile
+// work, unit-end flush, slot recycling, whole kernel, tiles.
+namespace mxs {
+__device__ unsigned long long g_str_clk[8];
+}
+extern "C" __attribute__((visibility("default"))) int mxs_prof_read_stream(unsigned long long* host, int clear) {
+    if (cudaMemcpyFromSymbol(host, mxs::g_str_clk, sizeof(mxs::g_str_clk)) != cudaSuccess) return -3;
+    if (clear) {
+        static unsigned long long zeros[8];
+        if (cudaMemcpyToSymbol(mxs::g_str_clk, zeros, sizeof(zeros)) != cudaSuccess) return -3;
+    }
+    return 0;
+}
+#define MXS_SCLK(v) long long v = clock64()
+#define MXS_SADD(i, x) do { if (warp == 0) sclk[i] += (unsigned long long)(x); } while (0)
+#else
+#define MXS_SCLK(v) (void)0
+#define MXS_SADD(i, x) (void)0
+#endif
+#ifdef MXS_PROFILE
 // Counters of the per-warp replays (profiling build): replays, heap build,
 // first-tile reads, list windows, final sort, draw (cycles summed over
 // replays).
@@ -170,6 +191,10 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
     }
 
     uint32_t* wk = wkeys + warp * SW_CAP;
+#ifdef MXS_PROFILE
+    unsigned long long sclk[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const long long k0 = clock64();
+#endif
     int32_t* wi = widx + warp * SW_CAP;
     const int m = (k + NWARPS - 1) / NWARPS;  // <= 16
     int s = 0;             // ring stage of the next tile
@@ -221,6 +246,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
         };
         const int a0 = c * TPC * S_TILE;  // the unit's first column (V < 2^31)
         const int last_len = (int)(V - (int64_t)(a0 + (nt - 1) * S_TILE));
+        float th_c = -INFINITY;  // cached prefix bound of the later tiles
         for (int t = 0; t < nt; ++t) {
             const int a = a0 + t * S_TILE;
             const int len = (t == nt - 1) ? last_len : S_TILE;
@@ -229,15 +255,19 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 fl |= FLAG_TIMEOUT;  // another warp's wait ran out: no more copies come
                 dead = true;
             }
+            MXS_SCLK(w0);
             if (!dead && !mbar_wait_bounded(&sm.full[s], parity)) {
                 fl |= FLAG_TIMEOUT;
                 dead = true;
                 *reinterpret_cast<volatile uint32_t*>(&sm.dead) = 1u;
             }
+            MXS_SCLK(w1);
+            MXS_SADD(1, w1 - w0);
+            MXS_SADD(7, 1);
             const float* st = ring + s * S_TILE;
             float vv[32];
             uint32_t valid = 0xFFFFFFFFu;
-            if (len == S_TILE) {
+            if (len >= (warp + 1) * 1024) {  // this warp's slice is whole (in the bulk copy)
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
                     const float4 f = *reinterpret_cast<const float4*>(st + 4 * (warp * 256 + lane + 32 * q));
@@ -327,8 +357,7 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 csync();
                 uint32_t mn = 0xFFFFFFFFu;
                 if (lane < NWARPS) mn = (uint32_t)*reinterpret_cast<volatile uint64_t*>(&us.pubh[lane][0]);
-#pragma unroll
-                for (int d = 16; d > 0; d >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, d));
+                mn = __reduce_min_sync(0xffffffffu, mn);
                 if (mn) seed = fmaxf(seed, bound_of(mn));
                 // x >= seed as a strict test (a seed of -inf lets -inf through
                 // as "not above": a row whose k-th largest is -inf then has too
@@ -343,18 +372,27 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 // latest publication from an earlier tile is used (the slots
                 // hold the last four, tagged; no warp runs more than two tiles
                 // ahead of another, so the one wanted is never overwritten).
-                uint32_t b = 0xFFFFFFFFu;
-                if (lane < NWARPS) {
-                    b = 0u;
+                // Bounds only grow, so an older one is valid too: a tile is
+                // first screened against the cached bound, and the current one
+                // is read only when something passes (or every fourth tile).
+                auto prefix_bound = [&]() -> float {
+                    uint32_t b = 0xFFFFFFFFu;
+                    if (lane < NWARPS) {
+                        b = 0u;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const uint64_t e = *reinterpret_cast<volatile uint64_t*>(&us.pubh[lane][q]);
-                        if ((int)(e >> 32) < t) b = max(b, (uint32_t)e);
+                        for (int q = 0; q < 4; ++q) {
+                            const uint64_t e = *reinterpret_cast<volatile uint64_t*>(&us.pubh[lane][q]);
+                            if ((int)(e >> 32) < t) b = max(b, (uint32_t)e);
+                        }
                     }
+                    return bound_of(__reduce_min_sync(0xffffffffu, b));
+                };
+                if (t == 1 || (t & 3) == 0) th_c = prefix_bound();
+                th = th_c;
+                if (__any_sync(0xffffffffu, mxn > th)) {
+                    th_c = prefix_bound();
+                    th = th_c;
                 }
-#pragma unroll
-                for (int d = 16; d > 0; d >>= 1) b = min(b, __shfl_xor_sync(0xffffffffu, b, d));
-                th = bound_of(b);
             }
             if (__any_sync(0xffffffffu, mxn > th)) {
                 uint32_t mm = 0;
@@ -451,6 +489,8 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                 }
             }
             if (t > 0) publish(t);
+            MXS_SCLK(te);
+            MXS_SADD(t == 0 ? 2 : 3, te - w1);
             // every lane of the warp is done with the stage: hand it back
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.empty[s])) : "memory");
@@ -460,10 +500,14 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             }
         }
         // Leave the unit: the rest of the buffer goes to the row's list.
+        MXS_SCLK(f0);
+        MXS_SADD(0, 1);
         flush();
         if (warp == 0) MXS_WCOUNT(6, 1);
         if (__any_sync(0xffffffffu, nan)) fl |= FLAG_NAN;
         if (lane == 0 && fl) atomicOr(&p.row_flag[row], fl);
+        MXS_SCLK(f1);
+        MXS_SADD(4, f1 - f0);
         // The last warp out recycles the slot for unit j + SLOTS (no warp can be
         // that far ahead: the ring keeps them within S_STAGES tiles of each other).
         __syncwarp();
@@ -489,7 +533,15 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             }
         }
         __syncwarp();
+        MXS_SCLK(f2);
+        MXS_SADD(5, f2 - f1);
     }
+#ifdef MXS_PROFILE
+    if (warp == 0 && lane == 0) {
+        sclk[6] = (unsigned long long)(clock64() - k0);
+        for (int i = 0; i < 8; ++i) atomicAdd(&g_str_clk[i], sclk[i]);
+    }
+#endif
 #ifdef MXS_PROFILE
     csync();  // consumers only: the counters are complete
     MXS_PROF_FLUSH();
