@@ -213,9 +213,10 @@ MXS_API int mxs_set_profile_events(void* start, void* stop);
  * GPU that loads it until the process exits; no call allocates or frees memory.
  * Returns MXS_ERR_WORKSPACE when the shape needs more scratch than that
  * (mxs_workspace_size tells how much). On the default path (top_k <= 128,
- * 16-byte aligned rows) the need is about rows x 8 KiB at any vocabulary, so
- * up to about 6,000 rows fit (the 4096-row batch of the throughput benchmark
- * does); top_k above 2048 needs the most (two k-entry slots per CTA).
+ * 16-byte aligned rows) the need is about rows x max(1024, 12 top_k + 512) x 8
+ * bytes at any vocabulary: about 5,600 rows fit at top_k = 50 (the 4096-row
+ * batch of the throughput benchmark does), about 3,000 at top_k = 128; top_k
+ * above 2048 needs the most (two k-entry slots per CTA).
  * Timeouts of these calls reach mxs_get_status like any other call's.
  * The first call on a device looks up the array's device address; make that
  * call before any stream capture. All calls share the one array, so calls
