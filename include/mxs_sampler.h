@@ -90,6 +90,36 @@ MXS_API int mxs_sample_topk_ex(const float* d_logits, int64_t rows, int64_t voca
                        int32_t* d_topk_idx, double* d_topk_prob, uint32_t* d_row_flags, void* d_workspace,
                        size_t workspace_bytes, void* stream);
 
+/*
+ * mxs_sample_topk_ex after the reference's pre-sampler edits on the device
+ * (src/api/minxfmr.cpp:2047-2089), applied in double as the reference does:
+ *   d_special[0, n_special)  token ids whose logits become -inf in every row
+ *                            (the reference's special tokens, EOS left out, as
+ *                            :2050-2055 skip it); ids outside the vocabulary
+ *                            are skipped
+ *   d_history, hist_stride, d_hist_len  row r's accepted tokens are
+ *                            d_history[r*hist_stride, + d_hist_len[r])
+ *   repeat_last_n, repeat_penalty, frequency_penalty, presence_penalty
+ *                            as minxfmr_generate: over the last repeat_last_n
+ *                            tokens (< 0: all), each distinct token's logit is
+ *                            multiplied (<= 0) or divided (> 0) by
+ *                            repeat_penalty and loses count*frequency_penalty +
+ *                            presence_penalty
+ * A penalised logit is a double fp32 cannot hold: the sampler carries it
+ * exactly (ids, tie order and probabilities as the reference's on the edited
+ * double logits). d_logits is edited in place: the masked and penalised
+ * tokens read -inf after the call. Limits: top_k <= 128, 16-byte aligned rows
+ * with ld % 4 == 0, a penalty window of at most 1024 tokens (else
+ * MXS_ERR_INVALID). A row holding a NaN logit is not drawn (next = -1,
+ * MXS_ROW_NAN). Library-owned workspace; asynchronous on `stream`.
+ */
+MXS_API int mxs_sample_topk_edits(float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
+                                  int top_k, double top_p, double min_p, const int32_t* d_special, int n_special,
+                                  const int32_t* d_history, int64_t hist_stride, const int32_t* d_hist_len,
+                                  int repeat_last_n, double repeat_penalty, double frequency_penalty,
+                                  double presence_penalty, const double* d_u, int32_t* d_next, int32_t* d_topk_idx,
+                                  double* d_topk_prob, uint32_t* d_row_flags, void* stream);
+
 /* Bytes of workspace mxs_sample_topk_ex needs for this shape on the current device. */
 MXS_API int mxs_workspace_size(int64_t rows, int64_t vocab, int top_k, size_t* bytes);
 

@@ -47,7 +47,9 @@ struct Device {
     size_t clean_off = 0;
     size_t ws_bytes = 0;
     HostBuffers hb;
-    std::mutex hb_mu;  // held for a whole host-buffer call: its buffers are reused by the next
+    std::mutex hb_mu;
+    void* edits = nullptr;  // edit lists of mxs_sample_topk_edits, grown on demand
+    size_t edits_bytes = 0;  // held for a whole host-buffer call: its buffers are reused by the next
 };
 
 std::mutex g_mu;
@@ -261,6 +263,88 @@ bool ws_ok(const void* ws, size_t bytes, size_t need) {
     return ws && (reinterpret_cast<uintptr_t>(ws) % 256 == 0) && bytes >= need;
 }
 
+// The reference's pre-sampler edits of one call (mxs_sample_topk_edits).
+struct EditSpec {
+    float* logits = nullptr;
+    const int32_t* special = nullptr;
+    int n_special = 0;
+    const int32_t* hist = nullptr;
+    int64_t hist_stride = 0;
+    const int32_t* hist_len = nullptr;
+    int repeat_last_n = 0;
+    double rp = 1.0, fp = 0.0, pp = 0.0;
+    int cap = 1;
+};
+
+int sample_impl(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature, int top_k,
+                double top_p, double min_p, const double* d_u, int32_t* d_next, int32_t* d_topk_idx,
+                double* d_topk_prob, uint32_t* d_row_flags, void* d_workspace, size_t workspace_bytes, void* stream,
+                const EditSpec* ed) {
+    if (rows < 0 || vocab <= 0 || vocab > INT32_MAX || ld < vocab) return MXS_ERR_INVALID;
+    if (rows == 0) return MXS_OK;
+    if (!d_logits || !d_u || !d_next) return MXS_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Device* d;
+    int rc = current_device(&d);
+    if (rc) return rc;
+    clamp_p(&top_p, &min_p);
+    const int k_use = clamp_k(top_k, vocab);
+    const Plan pl = make_plan(*d, rows, vocab, k_use, false, use_split(vocab, ld, d_logits, k_use));
+    void* ws = d_workspace;
+    if (!ws) {
+        rc = ensure_library_ws(*d, pl.total, (cudaStream_t)stream);
+        if (rc) return rc;
+        ws = d->ws;
+    } else if (!ws_ok(ws, workspace_bytes, pl.total)) {
+        return MXS_ERR_WORKSPACE;
+    }
+    Params p{};
+    p.logits = d_logits;
+    p.rows = rows;
+    p.vocab = vocab;
+    p.ld = ld;
+    p.temperature = temperature;
+    p.top_p = top_p;
+    p.min_p = min_p;
+    p.k_use = pl.k_use;
+    p.u = d_u;
+    p.next = d_next;
+    p.topk_idx = d_topk_idx;
+    p.topk_prob = d_topk_prob;
+    p.row_flags = d_row_flags;
+    p.mode = mxs::MODE_SAMPLE;
+    fill_workspace(p, pl, ws, *d);
+    if (ed) {
+        // the edit lists: [rows x cap] columns, [rows x cap] values, [rows] counts
+        const size_t cb = align_up(sizeof(int32_t) * (size_t)rows * ed->cap, 256);
+        const size_t vb = align_up(sizeof(double) * (size_t)rows * ed->cap, 256);
+        const size_t need = cb + vb + sizeof(uint32_t) * (size_t)rows;
+        if (d->edits_bytes < need) {
+            if (d->edits) {
+                if (cudaDeviceSynchronize() != cudaSuccess) return MXS_ERR_CUDA;  // earlier calls may still use it
+                cudaFree(d->edits);
+                d->edits = nullptr;
+                d->edits_bytes = 0;
+            }
+            if (cudaMalloc(&d->edits, need) != cudaSuccess) return MXS_ERR_CUDA;
+            d->edits_bytes = need;
+        }
+        char* eb = static_cast<char*>(d->edits);
+        int32_t* ecol = reinterpret_cast<int32_t*>(eb);
+        double* eval = reinterpret_cast<double*>(eb + cb);
+        uint32_t* ecnt = reinterpret_cast<uint32_t*>(eb + cb + vb);
+        if (mxs::edits_launch(ed->logits, rows, ld, vocab, ed->special, ed->n_special, ed->hist, ed->hist_stride,
+                              ed->hist_len, ed->repeat_last_n, ed->rp, ed->fp, ed->pp, ecol, eval, ecnt, ed->cap,
+                              (cudaStream_t)stream) != cudaSuccess)
+            return MXS_ERR_CUDA;
+        p.edit_col = ecol;
+        p.edit_val = eval;
+        p.edit_cnt = ecnt;
+        p.edit_cap = ed->cap;
+    }
+    return launch(p, pl, (cudaStream_t)stream, d->sms, d->ev_start, d->ev_stop, d_workspace ? nullptr : d);
+}
+
 }  // namespace
 
 namespace mxs {
@@ -349,41 +433,40 @@ int mxs_sample_topk_ex(const float* d_logits, int64_t rows, int64_t vocab, int64
                        int top_k, double top_p, double min_p, const double* d_u, int32_t* d_next,
                        int32_t* d_topk_idx, double* d_topk_prob, uint32_t* d_row_flags, void* d_workspace,
                        size_t workspace_bytes, void* stream) {
-    if (rows < 0 || vocab <= 0 || vocab > INT32_MAX || ld < vocab) return MXS_ERR_INVALID;
+    return sample_impl(d_logits, rows, vocab, ld, temperature, top_k, top_p, min_p, d_u, d_next, d_topk_idx,
+                       d_topk_prob, d_row_flags, d_workspace, workspace_bytes, stream, nullptr);
+}
+
+int mxs_sample_topk_edits(float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature, int top_k,
+                          double top_p, double min_p, const int32_t* d_special, int n_special,
+                          const int32_t* d_history, int64_t hist_stride, const int32_t* d_hist_len, int repeat_last_n,
+                          double repeat_penalty, double frequency_penalty, double presence_penalty, const double* d_u,
+                          int32_t* d_next, int32_t* d_topk_idx, double* d_topk_prob, uint32_t* d_row_flags,
+                          void* stream) {
+    if (rows < 0 || vocab <= 0 || vocab > INT32_MAX || ld < vocab || n_special < 0 || hist_stride < 0)
+        return MXS_ERR_INVALID;
     if (rows == 0) return MXS_OK;
-    if (!d_logits || !d_u || !d_next) return MXS_ERR_INVALID;
-    std::lock_guard<std::mutex> lk(g_mu);
-    Device* d;
-    int rc = current_device(&d);
-    if (rc) return rc;
-    clamp_p(&top_p, &min_p);
+    if (!d_logits || !d_u || !d_next || (n_special > 0 && !d_special) ||
+        (hist_stride > 0 && (!d_history || !d_hist_len)))
+        return MXS_ERR_INVALID;
+    const int64_t window = repeat_last_n < 0 ? hist_stride : std::min<int64_t>(repeat_last_n, hist_stride);
+    if (window > mxs::EDIT_WINDOW_MAX) return MXS_ERR_INVALID;
     const int k_use = clamp_k(top_k, vocab);
-    const Plan pl = make_plan(*d, rows, vocab, k_use, false, use_split(vocab, ld, d_logits, k_use));
-    void* ws = d_workspace;
-    if (!ws) {
-        rc = ensure_library_ws(*d, pl.total, (cudaStream_t)stream);
-        if (rc) return rc;
-        ws = d->ws;
-    } else if (!ws_ok(ws, workspace_bytes, pl.total)) {
-        return MXS_ERR_WORKSPACE;
-    }
-    Params p{};
-    p.logits = d_logits;
-    p.rows = rows;
-    p.vocab = vocab;
-    p.ld = ld;
-    p.temperature = temperature;
-    p.top_p = top_p;
-    p.min_p = min_p;
-    p.k_use = pl.k_use;
-    p.u = d_u;
-    p.next = d_next;
-    p.topk_idx = d_topk_idx;
-    p.topk_prob = d_topk_prob;
-    p.row_flags = d_row_flags;
-    p.mode = mxs::MODE_SAMPLE;
-    fill_workspace(p, pl, ws, *d);
-    return launch(p, pl, (cudaStream_t)stream, d->sms, d->ev_start, d->ev_stop, d_workspace ? nullptr : d);
+    if (!use_split(vocab, ld, d_logits, k_use)) return MXS_ERR_INVALID;  // top_k <= 128, 16-byte aligned rows
+    EditSpec ed;
+    ed.special = d_special;
+    ed.n_special = n_special;
+    ed.hist = d_history;
+    ed.hist_stride = hist_stride;
+    ed.hist_len = d_hist_len;
+    ed.repeat_last_n = repeat_last_n;
+    ed.rp = repeat_penalty;
+    ed.fp = frequency_penalty;
+    ed.pp = presence_penalty;
+    ed.cap = (int)std::max<int64_t>(1, window);
+    ed.logits = d_logits;
+    return sample_impl(d_logits, rows, vocab, ld, temperature, top_k, top_p, min_p, d_u, d_next, d_topk_idx,
+                       d_topk_prob, d_row_flags, nullptr, 0, stream, &ed);
 }
 
 int mxs_sample_topk(const float* d_logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,

@@ -242,4 +242,45 @@ __device__ __forceinline__ void pair_sort(PairHeap hp, int len) {
     }
 }
 
+// The same 1-based top-down heap over double values, for rows whose logits
+// were edited in double (penalties). 16-byte entries: a node's two children
+// are two adjacent 16-byte loads. No NaN.
+struct DEnt {
+    double v;
+    int32_t i;
+    int32_t pad;
+};
+
+__device__ __forceinline__ double dpair_place(DEnt* h, int hole, int len, DEnt e) {
+    const int top = hole;
+    double top_v = e.v;
+    for (;;) {
+        const int c = 2 * hole;
+        if (c > len) break;
+        const DEnt l = h[c];
+        const DEnt r = h[c + 1];  // read past len only within the array (len + 2 entries)
+        const bool right = (c + 1 <= len) && !(r.v > l.v);
+        const DEnt ch = right ? r : l;
+        if (ch.v > e.v) break;
+        h[hole] = ch;
+        if (hole == top) top_v = ch.v;
+        hole = c + (right ? 1 : 0);
+    }
+    h[hole] = e;
+    return top_v;
+}
+
+__device__ __forceinline__ void dpair_build(DEnt* h, int len) {
+    for (int p = len / 2; p >= 1; --p) dpair_place(h, p, len, h[p]);
+}
+
+__device__ __forceinline__ void dpair_sort(DEnt* h, int len) {
+    while (len > 1) {
+        const DEnt e = h[len];
+        h[len] = h[1];
+        --len;
+        dpair_place(h, 1, len, e);
+    }
+}
+
 }  // namespace mxs

@@ -78,6 +78,13 @@ struct Params {
     uint32_t* row_bound;       // rows: key of a lower bound of the row's k-th largest logit, from the
                                // streaming warps (0: none); cleared by the finish kernel
     int row_cap;
+    // pre-sampler edits (mxs_sample_topk_edits): per row, every penalised
+    // token's exact double value, sorted by column (their logits read -inf in
+    // the row, so the streaming pass never lists them); null edit_cnt: none
+    const int32_t* edit_col;   // rows x edit_cap
+    const double* edit_val;    // rows x edit_cap
+    const uint32_t* edit_cnt;  // rows
+    int edit_cap;
     int replay_warp_min;       // the finish kernel replays tie rows one per warp when its CTA holds at
                                // least this many of them, else with the whole CTA (MXS_REPLAY_WARP_MIN)
     int64_t debug_drop_tile;   // test hook (MXS_DEBUG_DROP_TILE): the streaming producer stops before

@@ -558,20 +558,51 @@ struct FinishWarpSmem {
     Ent e[KSPLIT_K];
     // the replay's heap, 1-based (pair_* in mxs_heap.cuh)
     alignas(16) Ent hp[KSPLIT_K + 2];
+    // the replay's heap over double values, for edited rows (dpair_*)
+    alignas(16) DEnt dh[KSPLIT_K + 2];
 };
+
+// The exact value of edited column `col` of row `row` (binary search of the
+// row's edit list, sorted by column).
+__device__ __forceinline__ double edit_value(const Params& p, int64_t row, int32_t col) {
+    const int32_t* c = p.edit_col + row * (int64_t)p.edit_cap;
+    int lo = 0, hi = (int)p.edit_cnt[row];
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (c[mid] < col) lo = mid + 1;
+        else hi = mid;
+    }
+    return p.edit_val[row * (int64_t)p.edit_cap + lo];
+}
+
+// An edited value as the float it is rounded down to, and whether that
+// float is inexact (then the value lies strictly between it and the next
+// float up, and bit 31 of the entry's column marks it).
+__device__ __forceinline__ float edit_float(double d, bool* inexact) {
+    const float f = __double2float_rd(d);
+    *inexact = (double)f != d;
+    return f;
+}
 
 // Draws for row `row` from e[0, k) and writes next (and the optional outputs);
 // returns the drawn position (in every lane).
-__device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, double* pbuf) {
+// Column bits of an Ent index: bit 31 marks a penalised logit whose double
+// value fp32 cannot hold (the entry's float is the value rounded down).
+constexpr int32_t COL_MASK = 0x7FFFFFFF;
+
+// dv (nullable): the entries' exact values, where penalised logits make the
+// floats inexact.
+__device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, double* pbuf,
+                         const double* dv = nullptr) {
     const int lane = threadIdx.x & 31;
     if (p.topk_idx)
-        for (int i = lane; i < k; i += 32) p.topk_idx[row * k + i] = e[i].i;
+        for (int i = lane; i < k; i += 32) p.topk_idx[row * k + i] = e[i].i & COL_MASK;
     const double T = p.temperature;
     bool greedy = (T <= 0.0);
     double sum = 0.0;
     if (!greedy) {
-        const double maxs = (double)e[0].v;
-        for (int i = lane; i < k; i += 32) pbuf[i] = exp(((double)e[i].v - maxs) / T);
+        const double maxs = dv ? dv[0] : (double)e[0].v;
+        for (int i = lane; i < k; i += 32) pbuf[i] = exp(((dv ? dv[i] : (double)e[i].v) - maxs) / T);
         __syncwarp();
         if (lane == 0) sum = seq_sum(pbuf, k);
         sum = __shfl_sync(0xffffffffu, sum, 0);
@@ -580,7 +611,7 @@ __device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, doub
     if (greedy) {
         if (p.topk_prob)
             for (int i = lane; i < k; i += 32) p.topk_prob[row * k + i] = (i == 0) ? 1.0 : 0.0;
-        if (lane == 0) p.next[row] = e[0].i;
+        if (lane == 0) p.next[row] = e[0].i & COL_MASK;
         return 0;
     }
     for (int i = lane; i < k; i += 32) {
@@ -599,7 +630,7 @@ __device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, doub
     s2 = __shfl_sync(0xffffffffu, s2, 0);
     __syncwarp();
     if (n < 2) {  // discrete_distribution with fewer than two weights returns 0
-        if (lane == 0) p.next[row] = e[0].i;
+        if (lane == 0) p.next[row] = e[0].i & COL_MASK;
         return 0;
     }
     for (int i = lane; i < n; i += 32) pbuf[i] = pbuf[i] / s2;
@@ -607,7 +638,7 @@ __device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, doub
     int pick = 0;
     if (lane == 0) {
         pick = cdf_pick(pbuf, n, p.u[row]);
-        p.next[row] = e[pick].i;
+        p.next[row] = e[pick].i & COL_MASK;
     }
     return __shfl_sync(0xffffffffu, pick, 0);
 }
@@ -644,14 +675,23 @@ __device__ __forceinline__ bool finish_sorted(const Params& p, int64_t row, Fini
 #pragma unroll
     for (int s2 = 0; s2 < NS; ++s2) any |= tm[s2];
     tie = tie || any != 0u;
-    if (tie && p.topk_idx) return true;
+    // With edited rows a key tie may hide an inexact double (bit 31): the
+    // double replay resolves every tie there.
+    if (tie && (p.topk_idx || p.edit_cnt)) return true;
 #pragma unroll
     for (int s2 = 0; s2 < NS; ++s2) {
         const int i = lane + 32 * s2;
         if (i < k) w.e[i] = Ent{fkey_inv((uint32_t)(b[s2] >> 32)), (int32_t)(uint32_t)b[s2]};
     }
     __syncwarp();
-    const int pick = warp_draw(p, row, w.e, k, w.pbuf);
+    double* dv = nullptr;
+    if (p.edit_cnt) {  // exact values of the k entries (the candidate buffer is free now)
+        dv = reinterpret_cast<double*>(w.keys);
+        for (int i = lane; i < k; i += 32)
+            dv[i] = (w.e[i].i < 0) ? edit_value(p, row, w.e[i].i & COL_MASK) : (double)w.e[i].v;
+        __syncwarp();
+    }
+    const int pick = warp_draw(p, row, w.e, k, w.pbuf, dv);
     uint32_t tp = 0u;
 #pragma unroll
     for (int s2 = 0; s2 < NS; ++s2)
@@ -866,6 +906,90 @@ __device__ void exact_row_warp_log(const Params& p, int64_t row, FinishWarpSmem&
     MXS_REP_T(q7);
     MXS_REP_ADD(4, q6 - q5);
     MXS_REP_ADD(5, q7 - q6);
+}
+
+// One warp replays the reference's heap process over an edited row in double,
+// reading the whole row once (512 logits per step) and merging the row's edit
+// list (sorted by column; those columns read -inf in memory) at its columns,
+// then draws. Rows without NaN; k <= KSPLIT_K. The heap lives in w.dh; w.keys /
+// w.idx hold the ordered list of logits above the root seen at the last offer.
+__device__ __forceinline__ void exact_row_warp_edits(const Params& p, int64_t row, FinishWarpSmem& w) {
+    const int lane = threadIdx.x & 31;
+    const int k = p.k_use;
+    const int64_t V = p.vocab;
+    const float* x = p.logits + row * p.ld;
+    const int32_t* ec = p.edit_col + row * (int64_t)p.edit_cap;
+    const double* ev = p.edit_val + row * (int64_t)p.edit_cap;
+    const int ne = (int)p.edit_cnt[row];
+    DEnt* h = w.dh;
+    Ent* slot = reinterpret_cast<Ent*>(w.keys);
+    int ecur = 0;  // the next edit to offer (lane 0's cursor)
+    for (int i = lane; i < k; i += 32) h[i + 1] = DEnt{(double)x[i], i, 0};
+    __syncwarp();
+    if (lane == 0) {
+        // edited columns inside the first k (node c + 1 holds column c before the build)
+        for (; ecur < ne && ec[ecur] < k; ++ecur) h[ec[ecur] + 1].v = ev[ecur];
+        dpair_build(h, k);
+    }
+    ecur = __shfl_sync(0xffffffffu, ecur, 0);
+    __syncwarp();
+    double r0 = h[1].v;
+    // lane 0: offer slot[0, c) in column order, each preceded by the edits of
+    // smaller columns; then the edits below `upto`
+    auto offer = [&](int c, int64_t upto) {
+        __syncwarp();
+        if (lane == 0) {
+            for (int j = 0; j <= c; ++j) {
+                const int64_t col = j < c ? (int64_t)slot[j].i : upto;
+                for (; ecur < ne && ec[ecur] < col; ++ecur)
+                    if (ev[ecur] > r0) r0 = dpair_place(h, 1, k, DEnt{ev[ecur], ec[ecur], 0});
+                if (j < c && (double)slot[j].v > r0) r0 = dpair_place(h, 1, k, DEnt{(double)slot[j].v, slot[j].i, 0});
+            }
+        }
+        r0 = __shfl_sync(0xffffffffu, r0, 0);
+        ecur = __shfl_sync(0xffffffffu, ecur, 0);
+    };
+    int c = 0;
+    const int64_t g0 = (int64_t)k & ~(int64_t)3;  // rows start 16-byte aligned on this path
+    for (int64_t g = g0; g < V; g += 512) {
+        float4 cur[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int64_t j = g + 128 * q + 4 * lane;
+            if (j < V) xload4(x, j, V, cur[q]);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (c > XSLOT - 128) {
+                offer(c, g + 128 * q);
+                c = 0;
+            }
+            const int64_t j = g + 128 * q + 4 * lane;
+            const float e4[4] = {cur[q].x, cur[q].y, cur[q].z, cur[q].w};
+            uint32_t m = 0u;
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                if (j + t >= k && j + t < V && (double)e4[t] > r0) m |= 1u << t;
+            const int n = __popc(m);
+            const int incl = warp_incl_scan(n);
+            int at = c + incl - n;
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                if (m & (1u << t)) slot[at++] = Ent{e4[t], (int32_t)(j + t)};
+            c += __shfl_sync(0xffffffffu, incl, 31);
+        }
+    }
+    offer(c, V);
+    if (lane == 0) dpair_sort(h, k);
+    __syncwarp();
+    double* dv = reinterpret_cast<double*>(w.keys);  // the list is offered: free
+    for (int i = lane; i < k; i += 32) {
+        w.e[i] = Ent{(float)h[i + 1].v, h[i + 1].i};
+        dv[i] = h[i + 1].v;
+    }
+    __syncwarp();
+    warp_draw(p, row, w.e, k, w.pbuf, dv);
+    __syncwarp();
 }
 
 // One warp finishes row `row`; returns true (in every lane) when the row needs
@@ -1129,6 +1253,37 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
     if (!(flags & FLAG_TIMEOUT) && !exact) {
         bool massive = false;
         int cnt = gather_row_list(p, row, w, cnt_all, k, &massive);
+        if (p.edit_cnt && !massive) {
+            // the edited (penalised) logits, which the streaming pass never
+            // saw: their floats rounded down, inexact ones marked in bit 31
+            const int ne = (int)p.edit_cnt[row];
+            const uint32_t lt = (1u << lane) - 1u;
+            uint32_t bound = 0u;
+            for (int j0 = 0; j0 < ne && !massive; j0 += 32) {
+                const int j = j0 + lane;
+                bool take = false;
+                uint32_t key = 0u;
+                int32_t col = 0;
+                if (j < ne) {
+                    bool inexact;
+                    key = fkey(edit_float(p.edit_val[row * (int64_t)p.edit_cap + j], &inexact));
+                    col = p.edit_col[row * (int64_t)p.edit_cap + j] | (inexact ? (int32_t)0x80000000 : 0);
+                    take = key >= bound;
+                }
+                const uint32_t bal = __ballot_sync(0xffffffffu, take);
+                if (take) {
+                    w.keys[cnt + __popc(bal & lt)] = key;
+                    w.idx[cnt + __popc(bal & lt)] = col;
+                }
+                cnt += __popc(bal);
+                __syncwarp();
+                if (cnt > FCAP - 32) {
+                    bound = warp_select_kth_small(w.keys, cnt, k);
+                    cnt = warp_compact_ge(w.keys, w.idx, cnt, bound);
+                    if (cnt > FCAP - 32) massive = true;
+                }
+            }
+        }
         exact = massive;
         // Ties among the survivors, or across the cut, make the reference's
         // order of the equal values a product of its heap process. The
@@ -1144,7 +1299,7 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
             cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
             if (cnt != k) {  // a tie straddles the cut
                 tie = true;
-                exact = (cnt > KSPLIT_K) || (p.topk_idx != nullptr);
+                exact = (cnt > KSPLIT_K) || (p.topk_idx != nullptr) || (p.edit_cnt != nullptr);
             }
         } else if (!exact && cnt < k) {
             exact = true;
@@ -1212,6 +1367,13 @@ __global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) 
     uint32_t flags = 0u, cnt_all = 0u;
     bool full = false;
     const bool need = row < p.rows && finish_row_warp(p, row, w, &flags, &cnt_all, &full);
+    if (p.edit_cnt) {
+        // Edited rows: every replay in double by the row's own warp; a row
+        // with a NaN is left without a draw (next = -1, MXS_ROW_NAN).
+        if (need && !(flags & FLAG_NAN)) exact_row_warp_edits(p, row, w);
+        if (need && (flags & FLAG_NAN) && lane == 0) p.next[row] = -1;
+        return;
+    }
     // A row whose list stands for it (no NaN, no overflow, at least k entries)
     // is replayed by its own warp from the list and its chunks' first tiles;
     // the others read the whole row with the CTA.
@@ -1260,7 +1422,8 @@ extern "C" __attribute__((visibility("default"))) int mxs_prof_read_finish(unsig
 // MODE_EMIT's second kernel: one warp per row writes the shard's candidate
 // list (its own kernel: the branch inside finish_rows_kernel slowed sampling).
 __global__ void __launch_bounds__(F_WARPS * 32) emit_rows_kernel(Params p) {
-    __shared__ FinishWarpSmem ws[F_WARPS];
+    extern __shared__ __align__(128) unsigned char esmem[];
+    FinishWarpSmem* ws = reinterpret_cast<FinishWarpSmem*>(esmem);
     const int warp = threadIdx.x >> 5;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int64_t row = (int64_t)blockIdx.x * F_WARPS + warp;
@@ -1460,6 +1623,101 @@ cudaError_t vocab_replay_merge_launch(const VocabReplayArgs& a, const Params& dr
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// The reference's pre-sampler edits (src/api/minxfmr.cpp:2047-2089), one CTA
+// per row: the special tokens' logits become -inf; each distinct token among
+// the row's last penalty_n accepted tokens gets, in double, the repetition
+// penalty (multiplied when <= 0, divided otherwise) and loses
+// count * frequency_penalty + presence_penalty. The penalised values go to the
+// row's edit list (sorted by column) and their logits to -inf, so the sampler
+// sees them only as doubles.
+// ---------------------------------------------------------------------------
+constexpr int EDIT_MAX = EDIT_WINDOW_MAX;
+
+__global__ void __launch_bounds__(256) edits_kernel(float* logits, int64_t ld, int64_t vocab, const int32_t* special,
+                                                    int n_special, const int32_t* hist, int64_t hist_stride,
+                                                    const int32_t* hist_len, int repeat_last_n, double rp, double fp,
+                                                    double pp, int32_t* edit_col, double* edit_val,
+                                                    uint32_t* edit_cnt, int edit_cap) {
+    __shared__ int32_t tok[EDIT_MAX];
+    __shared__ int wsum[8];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t r = blockIdx.x;
+    float* row = logits + r * ld;
+    int hl = hist_len ? hist_len[r] : 0;
+    hl = (int)min((int64_t)max(hl, 0), hist_stride);
+    int pn = repeat_last_n < 0 ? hl : min(repeat_last_n, hl);  // src/api/minxfmr.cpp:2061-2064
+    if (!(pn > 0 && (rp != 1.0 || fp != 0.0 || pp != 0.0))) pn = 0;
+    pn = min(pn, EDIT_MAX);
+    int P = 1;
+    while (P < pn) P <<= 1;
+    for (int i = tid; i < P; i += blockDim.x)
+        tok[i] = i < pn ? hist[r * hist_stride + (hl - pn) + i] : INT32_MAX;
+    __syncthreads();
+    for (int size = 2; size <= P; size <<= 1) {  // ascending bitonic sort
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < P / 2; i += blockDim.x) {
+                const int a = 2 * i - (i & (stride - 1)), b2 = a + stride;
+                const bool up = (a & size) == 0;
+                const int32_t x = tok[a], y = tok[b2];
+                if ((x > y) == up) {
+                    tok[a] = y;
+                    tok[b2] = x;
+                }
+            }
+            __syncthreads();
+        }
+    }
+    // run starts of distinct in-vocabulary tokens: one edit each
+    int base = 0;
+    for (int i0 = 0; i0 < pn; i0 += blockDim.x) {
+        const int i = i0 + tid;
+        const int32_t t = i < pn ? tok[i] : INT32_MAX;
+        const bool start = i < pn && (i == 0 || tok[i - 1] != t) && t >= 0 && t < vocab;
+        const uint32_t bal = __ballot_sync(0xffffffffu, start);
+        if (lane == 0) wsum[warp] = __popc(bal);
+        __syncthreads();
+        int before = base;
+        for (int w2 = 0; w2 < warp; ++w2) before += wsum[w2];
+        int total = 0;
+        for (int w2 = 0; w2 < 8; ++w2) total += wsum[w2];
+        if (start) {
+            int j = i + 1;
+            while (j < pn && tok[j] == t) ++j;
+            const int count = j - i;
+            bool masked = false;
+            for (int q = 0; q < n_special; ++q) masked |= special[q] == t;
+            double logit = masked ? -INFINITY : (double)row[t];
+            if (rp != 1.0) logit = (logit <= 0.0) ? logit * rp : logit / rp;
+            logit -= (double)count * fp + (count > 0 ? pp : 0.0);
+            const int at = before + __popc(bal & ((1u << lane) - 1u));
+            if (at < edit_cap) {
+                edit_col[r * (int64_t)edit_cap + at] = t;
+                edit_val[r * (int64_t)edit_cap + at] = logit;
+            }
+        }
+        __syncthreads();
+        base += total;
+    }
+    if (tid == 0) edit_cnt[r] = (uint32_t)min(base, edit_cap);
+    __syncthreads();  // every read of the row is done
+    for (int q = tid; q < n_special; q += blockDim.x) {
+        const int32_t t = special[q];
+        if (t >= 0 && t < vocab) row[t] = -INFINITY;
+    }
+    for (int i = tid; i < base && i < edit_cap; i += blockDim.x) row[edit_col[r * (int64_t)edit_cap + i]] = -INFINITY;
+}
+
+cudaError_t edits_launch(float* logits, int64_t rows, int64_t ld, int64_t vocab, const int32_t* special,
+                         int n_special, const int32_t* hist, int64_t hist_stride, const int32_t* hist_len,
+                         int repeat_last_n, double rp, double fp, double pp, int32_t* edit_col, double* edit_val,
+                         uint32_t* edit_cnt, int edit_cap, cudaStream_t stream) {
+    edits_kernel<<<(unsigned)rows, 256, 0, stream>>>(logits, ld, vocab, special, n_special, hist, hist_stride,
+                                                    hist_len, repeat_last_n, rp, fp, pp, edit_col, edit_val,
+                                                    edit_cnt, edit_cap);
+    return cudaGetLastError();
+}
+
 size_t stream_smem_bytes() { return S_SMEM; }
 
 cudaError_t merge_rows_launch(const Params& p, cudaStream_t stream) {
@@ -1474,7 +1732,7 @@ cudaError_t stream_path_configure(int* blocks_per_sm) {
     e = cudaFuncSetAttribute(finish_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F_SMEM);
     if (e != cudaSuccess) return e;
     for (const void* f : {(const void*)merge_rows_kernel, (const void*)vocab_replay_emit_kernel,
-                          (const void*)vocab_replay_merge_kernel}) {
+                          (const void*)vocab_replay_merge_kernel, (const void*)emit_rows_kernel}) {
         e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sizeof(FinishWarpSmem) * F_WARPS));
         if (e != cudaSuccess) return e;
     }
@@ -1489,7 +1747,8 @@ cudaError_t stream_path_launch(const Params& p, int grid, cudaStream_t stream, c
     if (ev_stop) cudaEventRecord(ev_stop, stream);
     if (e != cudaSuccess) return e;
     if (p.mode == MODE_EMIT) {
-        emit_rows_kernel<<<(unsigned)((p.rows + F_WARPS - 1) / F_WARPS), F_WARPS * 32, 0, stream>>>(p);
+        emit_rows_kernel<<<(unsigned)((p.rows + F_WARPS - 1) / F_WARPS), F_WARPS * 32, sizeof(FinishWarpSmem) * F_WARPS,
+                           stream>>>(p);
         return cudaGetLastError();
     }
     const int64_t rpc = p.rows <= FINISH_ONE_ROW_PER_CTA ? 1 : F_WARPS;

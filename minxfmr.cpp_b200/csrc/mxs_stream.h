@@ -1,6 +1,7 @@
 // Launch interface of the two-kernel path (mxs_stream.cu).
 #pragma once
 #include <cstddef>
+#include <cstdint>
 #include <cuda_runtime.h>
 
 namespace mxs {
@@ -12,6 +13,12 @@ constexpr int S_STAGES = 3;          // ring depth (96 KB in flight per CTA)
 size_t stream_smem_bytes();
 cudaError_t stream_path_configure(int* blocks_per_sm);
 cudaError_t merge_rows_launch(const Params& p, cudaStream_t stream);  // MODE_MERGE, k <= KSPLIT
+constexpr int EDIT_WINDOW_MAX = 1024;  // longest penalty window of mxs_sample_topk_edits
+// The reference's pre-sampler edits, one CTA per row (mxs_sample_topk_edits).
+cudaError_t edits_launch(float* logits, int64_t rows, int64_t ld, int64_t vocab, const int32_t* special,
+                         int n_special, const int32_t* hist, int64_t hist_stride, const int32_t* hist_len,
+                         int repeat_last_n, double rp, double fp, double pp, int32_t* edit_col, double* edit_val,
+                         uint32_t* edit_cnt, int edit_cap, cudaStream_t stream);
 
 // Vocab-sharded tie rows (mxs_multi.cu): the rows a merge handed back for
 // their tie order, resolved from lists instead of full rows.

@@ -38,7 +38,7 @@ EXPORTS = (
     "mxs_sample_topk", "mxs_sample_topk_ex", "mxs_workspace_size", "mxs_workspace_init",
     "mxs_sample_topk_host", "mxs_shard_candidates", "mxs_merge_sample", "mxs_get_status",
     "mxs_version", "mxs_sample_topk_noalloc", "mxs_set_profile_events", "mxs_sample_rowsharded",
-    "mxs_sample_vocabsharded", "mxs_set_test_hooks", "mxs_vocabsharded_stats",
+    "mxs_sample_vocabsharded", "mxs_set_test_hooks", "mxs_vocabsharded_stats", "mxs_sample_topk_edits",
 )
 
 _P = ctypes.c_void_p
@@ -63,6 +63,8 @@ _SIGS = {
     "mxs_sample_vocabsharded": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _P, _P],
     "mxs_set_test_hooks": [_I64, _I, _I],
     "mxs_vocabsharded_stats": [ctypes.POINTER(_I64), ctypes.POINTER(_I64)],
+    "mxs_sample_topk_edits": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _I, _P, _I64, _P, _I, _D, _D, _D, _P, _P,
+                              _P, _P, _P, _P],
 }
 
 _lib = None
@@ -154,6 +156,38 @@ def sample(logits, temperature, top_k, u, top_p=1.0, min_p=0.0, out=None, return
                                     _ptr(idx), _ptr(prob), _ptr(flags), ws_ptr, ws_bytes,
                                     _stream(stream))
     _check("mxs_sample_topk_ex", rc)
+    if return_flags:
+        return nxt, idx, prob, flags
+    return nxt, idx, prob
+
+
+def sample_edits(logits, temperature, top_k, u, special=None, history=None, history_len=None, repeat_last_n=64,
+                 repeat_penalty=1.0, frequency_penalty=0.0, presence_penalty=0.0, top_p=1.0, min_p=0.0,
+                 return_flags=False, stream=None):
+    """sample() after the reference's pre-sampler edits, on the device
+    (mxs_sample_topk_edits): `special` [n] int32 token ids masked to -inf,
+    `history` [rows, stride] int32 accepted tokens with `history_len` [rows]
+    int32, and the repetition / frequency / presence penalties over the last
+    repeat_last_n of them, in double as the reference applies them. `logits`
+    is edited in place (masked and penalised tokens read -inf afterwards)."""
+    _need_cuda(logits, "logits", torch.float32)
+    _need_cuda(u, "u", torch.float64)
+    rows, vocab = logits.shape
+    k = k_use(int(top_k), vocab)
+    dev = logits.device
+    nxt = torch.empty(rows, dtype=torch.int32, device=dev)
+    idx = torch.empty((rows, k), dtype=torch.int32, device=dev)
+    prob = torch.empty((rows, k), dtype=torch.float64, device=dev)
+    flags = torch.empty(rows, dtype=torch.int32, device=dev)
+    n_special = 0 if special is None else special.numel()
+    stride = 0 if history is None else history.shape[1]
+    with torch.cuda.device(dev):
+        rc = load().mxs_sample_topk_edits(_ptr(logits), rows, vocab, logits.stride(0), float(temperature),
+                                          int(top_k), float(top_p), float(min_p), _ptr(special), n_special,
+                                          _ptr(history), stride, _ptr(history_len), int(repeat_last_n),
+                                          float(repeat_penalty), float(frequency_penalty), float(presence_penalty),
+                                          _ptr(u), _ptr(nxt), _ptr(idx), _ptr(prob), _ptr(flags), _stream(stream))
+    _check("mxs_sample_topk_edits", rc)
     if return_flags:
         return nxt, idx, prob, flags
     return nxt, idx, prob

@@ -4,9 +4,12 @@ The reference keeps its sampler inline in minxfmr_generate
 (src/api/minxfmr.cpp:2091-2171), so it cannot be linked on its own. This script
 copies exactly that block -- from the line `int k_use = top_k;` up to, not
 including, `std::string raw_tok = tokenizer_id_to_token(next);` -- out of the
-reference tree into oracle/_ref/sampler_block.inc, which ref_harness.cpp
-#includes inside a function that declares the same local variables. The slice
-stays in oracle/_ref/ (git-ignored); nothing from the reference is committed.
+reference tree into oracle/_ref/sampler_block.inc, and the pre-sampler edits
+before it (special-token mask and penalties, src/api/minxfmr.cpp:2047-2089:
+from the comment line that opens them up to `int k_use = top_k;`) into
+oracle/_ref/edits_block.inc. ref_harness.cpp #includes them inside functions
+that declare the same local variables. The slices stay in oracle/_ref/
+(git-ignored); nothing from the reference is committed.
 
 Usage: python oracle/extract_ref_block.py <reference_root> <out_dir>
 Exit status 2 when the reference is absent or the anchors are not found.
@@ -16,6 +19,7 @@ import os
 import sys
 
 START = "int k_use = top_k;"
+EDITS_START = "// Suppress non-EOS special/control tokens to avoid template leakage and"
 END = "std::string raw_tok = tokenizer_id_to_token(next);"
 REL = os.path.join("src", "api", "minxfmr.cpp")
 
@@ -41,6 +45,17 @@ def main(argv):
         f.write(f"// sliced from {REL}:{starts[0] + 1}-{ends[0]} sha256:{digest}\n")
         f.write(body)
     print(f"{REL}:{starts[0] + 1}-{ends[0]} ({len(block)} lines) sha256:{digest}")
+    e0 = [i for i, l in enumerate(lines) if l.strip() == EDITS_START]
+    if len(e0) != 1 or e0[0] >= starts[0]:
+        print(f"edit-block anchor not found exactly once in {src}", file=sys.stderr)
+        return 2
+    edits = lines[e0[0]:starts[0]]
+    body = "\n".join(edits) + "\n"
+    digest = hashlib.sha256(body.encode()).hexdigest()[:16]
+    with open(os.path.join(out_dir, "edits_block.inc"), "w") as f:
+        f.write(f"// sliced from {REL}:{e0[0] + 1}-{starts[0]} sha256:{digest}\n")
+        f.write(body)
+    print(f"{REL}:{e0[0] + 1}-{starts[0]} ({len(edits)} lines) sha256:{digest}")
     return 0
 
 

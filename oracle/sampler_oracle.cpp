@@ -65,8 +65,9 @@ namespace {
 // logits[a] > logits[b] (src/api/minxfmr.cpp:2102). A heap ordered by it keeps
 // the smallest value at the root.
 // ---------------------------------------------------------------------------
+template <typename T>
 struct HeapRow {
-    const float* x;
+    const T* x;
     int32_t* h;  // heap of indices
     bool before(int32_t a, int32_t b) const { return x[a] > x[b]; }
 
@@ -119,8 +120,9 @@ struct HeapRow {
     }
 };
 
-void restated_partial_sort(const float* x, int64_t vocab, int64_t k, int32_t* order, bool top_down = false) {
-    HeapRow hr{x, order};
+template <typename T>
+void restated_partial_sort(const T* x, int64_t vocab, int64_t k, int32_t* order, bool top_down = false) {
+    HeapRow<T> hr{x, order};
     if (top_down)
         for (int64_t i = 0; i < vocab; ++i)
             if (x[i] != x[i]) top_down = false;
@@ -162,12 +164,10 @@ int64_t lower_bound_cp(const double* cp, int64_t n, double u) {
     return first;
 }
 
-struct RowOut {
-    int32_t next;
-};
-
-// One row of the sampling block. order must hold vocab ints; probs/cp k_use doubles.
-int32_t sample_row(const float* x, int64_t vocab, double temperature, int top_k, double top_p,
+// One row of the sampling block (fp32 logits, or the double logits a row has
+// after the pre-sampler edits). order must hold vocab ints; probs/cp k_use doubles.
+template <typename T>
+int32_t sample_row(const T* x, int64_t vocab, double temperature, int top_k, double top_p,
                    double min_p, double u, int mode, int32_t* order, double* probs, double* cp,
                    int32_t* topk_idx, double* topk_prob) {
     int64_t k_use = top_k <= 0 ? 1 : top_k;
@@ -278,6 +278,83 @@ int mxs_oracle_sample(const float* logits, int64_t rows, int64_t vocab, int64_t 
             next[r] = sample_row(logits + r * ld, vocab, temperature, top_k, top_p, min_p, u[r],
                                  mode, order.data(), probs.data(), cp.data(),
                                  topk_idx ? topk_idx + r * k_use : nullptr,
+                                 topk_prob ? topk_prob + r * k_use : nullptr);
+        }
+    }
+    (void)threads;
+    return (int)k_use;
+}
+
+// The reference's pre-sampler edits (src/api/minxfmr.cpp:2047-2089), on one
+// row widened to double: the special tokens' logits become -inf (the caller
+// passes their ids, EOS already left out, as :2050-2055 skip it), then, over
+// the last penalty_n accepted tokens (repeat_last_n < 0: all of them; at most
+// the history length), each distinct token's logit gets the repetition
+// penalty (multiplied when <= 0, divided otherwise) and loses
+// count * frequency_penalty + presence_penalty, in double. Tokens outside the
+// vocabulary are skipped.
+void apply_edits(double* row, int64_t vocab, const int32_t* special, int n_special, const int32_t* hist,
+                 int hist_len, int repeat_last_n, double repeat_penalty, double frequency_penalty,
+                 double presence_penalty) {
+    for (int i = 0; i < n_special; ++i) {
+        const int32_t sid = special[i];
+        if (sid < 0 || sid >= vocab) continue;
+        row[sid] = -std::numeric_limits<double>::infinity();
+    }
+    int penalty_n = repeat_last_n;
+    if (penalty_n < 0) penalty_n = hist_len;
+    if (penalty_n > hist_len) penalty_n = hist_len;
+    if (penalty_n <= 0 || (repeat_penalty == 1.0 && frequency_penalty == 0.0 && presence_penalty == 0.0)) return;
+    std::vector<int32_t> toks(hist + (hist_len - penalty_n), hist + hist_len);
+    std::sort(toks.begin(), toks.end());
+    for (size_t i = 0; i < toks.size();) {
+        size_t j = i;
+        while (j < toks.size() && toks[j] == toks[i]) ++j;
+        const int32_t tid = toks[i];
+        const int count = (int)(j - i);
+        i = j;
+        if (tid < 0 || tid >= vocab) continue;
+        double logit = row[tid];
+        if (repeat_penalty != 1.0) {
+            if (logit <= 0.0)
+                logit *= repeat_penalty;
+            else
+                logit /= repeat_penalty;
+        }
+        logit -= (double)count * frequency_penalty + (count > 0 ? presence_penalty : 0.0);
+        row[tid] = logit;
+    }
+}
+
+// mxs_oracle_sample after the pre-sampler edits: special token ids (shared by
+// every row), and per row its accepted tokens hist[r * hist_stride, + hist_len[r]).
+int mxs_oracle_sample_edits(const float* logits, int64_t rows, int64_t vocab, int64_t ld, double temperature,
+                            int top_k, double top_p, double min_p, const double* u, const int32_t* special,
+                            int n_special, const int32_t* hist, int64_t hist_stride, const int32_t* hist_len,
+                            int repeat_last_n, double repeat_penalty, double frequency_penalty,
+                            double presence_penalty, int32_t* next, int32_t* topk_idx, double* topk_prob, int mode,
+                            int threads) {
+    if (!logits || !u || !next || rows < 0 || vocab <= 0 || ld < vocab) return -1;
+    int64_t k_use = top_k <= 0 ? 1 : top_k;
+    if (k_use > vocab) k_use = vocab;
+#ifdef _OPENMP
+    if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel num_threads(threads)
+#endif
+    {
+        std::vector<int32_t> order((size_t)vocab);
+        std::vector<double> row((size_t)vocab), probs((size_t)k_use), cp((size_t)k_use);
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+        for (int64_t r = 0; r < rows; ++r) {
+            const float* src = logits + r * ld;
+            for (int64_t i = 0; i < vocab; ++i) row[(size_t)i] = (double)src[i];
+            apply_edits(row.data(), vocab, special, n_special, hist ? hist + r * hist_stride : nullptr,
+                        hist_len ? hist_len[r] : 0, repeat_last_n, repeat_penalty, frequency_penalty,
+                        presence_penalty);
+            next[r] = sample_row(row.data(), vocab, temperature, top_k, top_p, min_p, u[r], mode, order.data(),
+                                 probs.data(), cp.data(), topk_idx ? topk_idx + r * k_use : nullptr,
                                  topk_prob ? topk_prob + r * k_use : nullptr);
         }
     }

@@ -41,6 +41,9 @@ def oracle():
         lib.mxs_oracle_uniforms.argtypes = [ctypes.c_uint32, _I64, _P]
         lib.mxs_oracle_check_draw.argtypes = [ctypes.c_uint32, _P, _I64, _P, _P]
         lib.mxs_oracle_topk_order.argtypes = [_P, _I64, _I, _I, _P]
+        lib.mxs_oracle_sample_edits.argtypes = [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _I, _P, _I64, _P,
+                                                _I, _D, _D, _D, _P, _P, _P, _I, _I]
+        lib.mxs_oracle_sample_edits.restype = _I
         _oracle = lib
     return _oracle
 
@@ -56,6 +59,9 @@ def ref():
         lib.mxs_ref_sample.argtypes = [_P, _I64, _I64, _I64, _D, _I, _D, _D, ctypes.c_uint32,
                                        _P, _P, _P, _P, _I]
         lib.mxs_ref_sample.restype = _I
+        lib.mxs_ref_sample_edits.argtypes = [_P, _I64, _I64, _I64, _D, _I, _D, _D, ctypes.c_uint32, _P, _I, _P,
+                                             _I64, _P, _I, _D, _D, _D, _P, _P, _P, _P, _I]
+        lib.mxs_ref_sample_edits.restype = _I
         _ref = lib
     return _ref
 
@@ -110,3 +116,54 @@ def topk_order(x, top_k, mode):
     out = np.empty(k, np.int32)
     oracle().mxs_oracle_topk_order(_ptr(x), x.shape[0], int(top_k), mode, _ptr(out))
     return out
+
+
+class Edits:
+    """The reference's pre-sampler edits (src/api/minxfmr.cpp:2047-2089):
+    special token ids masked to -inf in every row, then repetition /
+    frequency / presence penalties over the last repeat_last_n tokens of each
+    row's history (hist [rows, stride] int32, hist_len [rows] int32)."""
+
+    def __init__(self, special, hist, hist_len, repeat_last_n=64, repeat_penalty=1.0, frequency_penalty=0.0,
+                 presence_penalty=0.0):
+        self.special = np.ascontiguousarray(special, dtype=np.int32)
+        self.hist = np.ascontiguousarray(hist, dtype=np.int32)
+        self.hist_len = np.ascontiguousarray(hist_len, dtype=np.int32)
+        self.repeat_last_n = int(repeat_last_n)
+        self.repeat_penalty = float(repeat_penalty)
+        self.frequency_penalty = float(frequency_penalty)
+        self.presence_penalty = float(presence_penalty)
+
+    def args(self):
+        return (_ptr(self.special), len(self.special), _ptr(self.hist), self.hist.shape[1], _ptr(self.hist_len),
+                self.repeat_last_n, self.repeat_penalty, self.frequency_penalty, self.presence_penalty)
+
+
+def oracle_sample_edits(logits, temperature, top_k, u, edits, top_p=1.0, min_p=0.0, mode=0, threads=0):
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    rows, vocab = logits.shape
+    k = k_use(top_k, vocab)
+    nxt = np.empty(rows, np.int32)
+    idx = np.empty((rows, k), np.int32)
+    prob = np.empty((rows, k), np.float64)
+    u = np.ascontiguousarray(u, dtype=np.float64)
+    rc = oracle().mxs_oracle_sample_edits(_ptr(logits), rows, vocab, vocab, float(temperature), int(top_k),
+                                          float(top_p), float(min_p), _ptr(u), *edits.args(), _ptr(nxt),
+                                          _ptr(idx), _ptr(prob), mode, threads)
+    assert rc == k, rc
+    return nxt, idx, prob
+
+
+def ref_sample_edits(logits, temperature, top_k, seed, edits, top_p=1.0, min_p=0.0, threads=0):
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    rows, vocab = logits.shape
+    k = k_use(top_k, vocab)
+    nxt = np.empty(rows, np.int32)
+    idx = np.empty((rows, k), np.int32)
+    prob = np.full((rows, k), np.nan, np.float64)
+    plen = np.empty(rows, np.int32)
+    rc = ref().mxs_ref_sample_edits(_ptr(logits), rows, vocab, vocab, float(temperature), int(top_k), float(top_p),
+                                    float(min_p), seed & 0xFFFFFFFF, *edits.args(), _ptr(nxt), _ptr(idx),
+                                    _ptr(prob), _ptr(plen), threads)
+    assert rc == k, rc
+    return nxt, idx, prob, plen
