@@ -120,6 +120,26 @@ MXS_API int mxs_sample_topk_edits(float* d_logits, int64_t rows, int64_t vocab, 
                                   double presence_penalty, const double* d_u, int32_t* d_next, int32_t* d_topk_idx,
                                   double* d_topk_prob, uint32_t* d_row_flags, void* stream);
 
+/*
+ * The reference's checks on the sampled token, after a sampling call on the
+ * same stream (src/api/minxfmr.cpp:2189-2205 first-token fallback, :2232-2243
+ * EOS stop). The tokenizer stays with the caller, which classifies every
+ * token id once in d_token_class[vocab]:
+ *   MXS_TOKEN_NOT_FIRST  not usable as a row's first generated token (its
+ *                        rendered piece is empty or white space, or it is EOS
+ *                        or a role token: the reference's condition at :2189)
+ *   MXS_TOKEN_EOS        EOS (:2232)
+ * For rows with d_first_step[r] != 0 whose d_next is NOT_FIRST, d_next becomes
+ * the first token of d_topk_idx[r][1, k_use) that is not (unchanged if none
+ * is). d_stop[r] (nullable) gets 1 when the final d_next is EOS. d_topk_idx
+ * (rows x k_use, from the sampling call) may be NULL when d_first_step is.
+ */
+#define MXS_TOKEN_NOT_FIRST 1u
+#define MXS_TOKEN_EOS 2u
+MXS_API int mxs_token_checks(int64_t rows, int top_k, int64_t vocab, const int32_t* d_topk_idx, int32_t* d_next,
+                             const uint8_t* d_token_class, const uint8_t* d_first_step, uint8_t* d_stop,
+                             void* stream);
+
 /* Bytes of workspace mxs_sample_topk_ex needs for this shape on the current device. */
 MXS_API int mxs_workspace_size(int64_t rows, int64_t vocab, int top_k, size_t* bytes);
 

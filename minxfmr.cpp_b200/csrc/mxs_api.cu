@@ -263,6 +263,35 @@ bool ws_ok(const void* ws, size_t bytes, size_t need) {
     return ws && (reinterpret_cast<uintptr_t>(ws) % 256 == 0) && bytes >= need;
 }
 
+// The reference's checks on the sampled token (src/api/minxfmr.cpp:2189-2205,
+// :2232-2243), one warp per row: on a row's first generated token, a token the
+// caller's table marks unusable as a first token (an invisible piece, EOS or
+// a role token) is replaced by the first usable one of order[1, k); then the
+// row's stop flag says whether the token is EOS.
+__global__ void token_checks_kernel(int64_t rows, int k, const int32_t* order, int32_t* next, const uint8_t* cls,
+                                    int64_t vocab, const uint8_t* first_step, uint8_t* stop) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    auto bad_first = [&](int32_t t) { return t < 0 || t >= vocab || (cls[t] & MXS_TOKEN_NOT_FIRST); };
+    int32_t nx = next[r];
+    if (first_step && first_step[r] && bad_first(nx)) {
+        for (int i0 = 1; i0 < k; i0 += 32) {
+            const int i = i0 + lane;
+            const int32_t alt = i < k ? order[r * k + i] : -1;
+            const uint32_t ok = __ballot_sync(0xffffffffu, i < k && !bad_first(alt));
+            if (ok) {
+                nx = __shfl_sync(0xffffffffu, alt, __ffs(ok) - 1);
+                break;
+            }
+        }
+    }
+    if (lane == 0) {
+        next[r] = nx;
+        if (stop) stop[r] = (nx >= 0 && nx < vocab && (cls[nx] & MXS_TOKEN_EOS)) ? 1 : 0;
+    }
+}
+
 // The reference's pre-sampler edits of one call (mxs_sample_topk_edits).
 struct EditSpec {
     float* logits = nullptr;
@@ -616,6 +645,17 @@ int mxs_merge_sample(const uint64_t* d_cand_all, const uint32_t* d_count_all, co
     p.outcap = 0;
     if (mxs::sample_kernel_launch(p, pl.grid, false, (cudaStream_t)stream) != cudaSuccess) return MXS_ERR_CUDA;
     return MXS_OK;
+}
+
+int mxs_token_checks(int64_t rows, int top_k, int64_t vocab, const int32_t* d_topk_idx, int32_t* d_next,
+                     const uint8_t* d_token_class, const uint8_t* d_first_step, uint8_t* d_stop, void* stream) {
+    if (rows < 0 || vocab <= 0 || vocab > INT32_MAX) return MXS_ERR_INVALID;
+    if (rows == 0) return MXS_OK;
+    if (!d_next || !d_token_class || (d_first_step && !d_topk_idx)) return MXS_ERR_INVALID;
+    const int k_use = clamp_k(top_k, vocab);
+    token_checks_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+        rows, k_use, d_topk_idx, d_next, d_token_class, vocab, d_first_step, d_stop);
+    return cudaGetLastError() == cudaSuccess ? MXS_OK : MXS_ERR_CUDA;
 }
 
 int mxs_set_profile_events(void* start, void* stop) {

@@ -32,6 +32,8 @@ ROW_EXACT = 1
 ROW_NAN = 2
 ROW_OVERFLOW = 4
 ROW_TIMEOUT = 8
+TOKEN_NOT_FIRST = 1
+TOKEN_EOS = 2
 
 # Every symbol include/mxs_sampler.h declares.
 EXPORTS = (
@@ -39,6 +41,7 @@ EXPORTS = (
     "mxs_sample_topk_host", "mxs_shard_candidates", "mxs_merge_sample", "mxs_get_status",
     "mxs_version", "mxs_sample_topk_noalloc", "mxs_set_profile_events", "mxs_sample_rowsharded",
     "mxs_sample_vocabsharded", "mxs_set_test_hooks", "mxs_vocabsharded_stats", "mxs_sample_topk_edits",
+    "mxs_token_checks",
 )
 
 _P = ctypes.c_void_p
@@ -63,6 +66,7 @@ _SIGS = {
     "mxs_sample_vocabsharded": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _P, _P],
     "mxs_set_test_hooks": [_I64, _I, _I],
     "mxs_vocabsharded_stats": [ctypes.POINTER(_I64), ctypes.POINTER(_I64)],
+    "mxs_token_checks": [_I64, _I, _I64, _P, _P, _P, _P, _P, _P],
     "mxs_sample_topk_edits": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _I, _P, _I64, _P, _I, _D, _D, _D, _P, _P,
                               _P, _P, _P, _P],
 }
@@ -191,6 +195,22 @@ def sample_edits(logits, temperature, top_k, u, special=None, history=None, hist
     if return_flags:
         return nxt, idx, prob, flags
     return nxt, idx, prob
+
+
+def token_checks(nxt, topk_idx, token_class, first_step=None, stream=None):
+    """mxs_token_checks on a sampling call's outputs: the first-token fallback
+    for rows with first_step (uint8 [rows]) set, in place on `nxt`; returns the
+    rows' EOS stop flags (uint8 [rows]). token_class: uint8 [vocab] of
+    TOKEN_NOT_FIRST / TOKEN_EOS bits."""
+    rows = nxt.numel()
+    vocab = token_class.numel()
+    k = topk_idx.shape[1] if topk_idx is not None else 1
+    stop = torch.empty(rows, dtype=torch.uint8, device=nxt.device)
+    with torch.cuda.device(nxt.device):
+        rc = load().mxs_token_checks(rows, k, vocab, _ptr(topk_idx), _ptr(nxt), _ptr(token_class), _ptr(first_step),
+                                     _ptr(stop), _stream(stream))
+    _check("mxs_token_checks", rc)
+    return stop
 
 
 def sample_noalloc(logits, temperature, top_k, u, top_p=1.0, min_p=0.0, out=None, stream=None):

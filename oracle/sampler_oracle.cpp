@@ -362,6 +362,28 @@ int mxs_oracle_sample_edits(const float* logits, int64_t rows, int64_t vocab, in
     return (int)k_use;
 }
 
+// The reference's checks on the sampled token (src/api/minxfmr.cpp:2189-2205,
+// :2232-2243) with the tokenizer's answers given per id in cls (bit 0: not
+// usable as a first token -- invisible piece, EOS or role token; bit 1: EOS):
+// on a row's first generated token a bit-0 token is replaced by the first
+// order[1, k) token without bit 0; stop[r] = the final token is EOS.
+void mxs_oracle_token_checks(int64_t rows, int64_t k, int64_t vocab, const int32_t* order, int32_t* next,
+                             const uint8_t* cls, const uint8_t* first_step, uint8_t* stop) {
+    auto bad_first = [&](int32_t t) { return t < 0 || t >= vocab || (cls[t] & 1u); };
+    for (int64_t r = 0; r < rows; ++r) {
+        if (first_step && first_step[r] && bad_first(next[r])) {
+            for (int64_t i = 1; i < k; ++i) {
+                const int32_t alt = order[r * k + i];
+                if (!bad_first(alt)) {
+                    next[r] = alt;
+                    break;
+                }
+            }
+        }
+        if (stop) stop[r] = (next[r] >= 0 && next[r] < vocab && (cls[next[r]] & 2u)) ? 1 : 0;
+    }
+}
+
 // u[r] = the double std::discrete_distribution<int> draws from
 // std::mt19937(seed + r): generate_canonical<double, 53> over two 32-bit outputs.
 void mxs_oracle_uniforms(uint32_t seed, int64_t n, double* out) {

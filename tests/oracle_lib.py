@@ -44,6 +44,7 @@ def oracle():
         lib.mxs_oracle_sample_edits.argtypes = [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _I, _P, _I64, _P,
                                                 _I, _D, _D, _D, _P, _P, _P, _I, _I]
         lib.mxs_oracle_sample_edits.restype = _I
+        lib.mxs_oracle_token_checks.argtypes = [_I64, _I64, _I64, _P, _P, _P, _P, _P]
         _oracle = lib
     return _oracle
 
@@ -167,3 +168,15 @@ def ref_sample_edits(logits, temperature, top_k, seed, edits, top_p=1.0, min_p=0
                                     _ptr(prob), _ptr(plen), threads)
     assert rc == k, rc
     return nxt, idx, prob, plen
+
+
+def token_checks(nxt, order, cls, first_step):
+    """The oracle's first-token fallback and EOS flags: returns (next, stop)."""
+    nxt = np.array(nxt, dtype=np.int32)
+    order = np.ascontiguousarray(order, dtype=np.int32)
+    cls = np.ascontiguousarray(cls, dtype=np.uint8)
+    first_step = np.ascontiguousarray(first_step, dtype=np.uint8)
+    stop = np.empty(len(nxt), np.uint8)
+    oracle().mxs_oracle_token_checks(len(nxt), order.shape[1], len(cls), _ptr(order), _ptr(nxt), _ptr(cls),
+                                     _ptr(first_step), _ptr(stop))
+    return nxt, stop
