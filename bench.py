@@ -330,6 +330,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-vocab", action="store_true", help="skip the vocab-sharded sub-record (N > 1)")
+    ap.add_argument("--no-ties", action="store_true", help="skip the tie-heavy sub-record (N = 1)")
     ap.add_argument("--mode", default="row", choices=["row", "vocab"],
                     help="row: the headline (row-sharded, weak scaling); vocab: vocab-sharded over NCCL")
     args = ap.parse_args()
@@ -427,6 +428,45 @@ def main():
                "steps": n_e2e, "timing": "host wall clock around synchronous calls (max over ranks)"}
         del h_logits
 
+    # Tie-heavy throughput (N = 1): the same rows rounded to bf16 (ties inside
+    # nearly every row's top-k; every row takes the heap replay from its list),
+    # and BASELINE's tie/large-k configuration (256 x 151,936 standard Gumbel
+    # quantised to 1/16, k = 1024). CUDA events around `reps` calls each.
+    ties = None
+    if world == 1 and not args.no_ties:
+        def timed(fn, reps):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(reps):
+                fn()
+            b.record(stream)
+            torch.cuda.synchronize()
+            return a.elapsed_time(b) / reps
+        lg16 = logits.bfloat16().float()
+        ms16 = timed(lambda: mxs_sampler.sample(lg16, TEMPERATURE, TOP_K, u, out=out, return_topk=False,
+                                                stream=stream), 10)
+        idx16 = torch.empty((rows, TOP_K), dtype=torch.int32, device=dev)
+        prob16 = torch.empty((rows, TOP_K), dtype=torch.float64, device=dev)
+        ms16k = timed(lambda: mxs_sampler.sample(lg16, TEMPERATURE, TOP_K, u, out=(nxt, idx16, prob16, None),
+                                                 stream=stream), 10)
+        del lg16, idx16, prob16
+        g4 = torch.Generator(device=dev)
+        g4.manual_seed(44)
+        c4 = -torch.log(-torch.log(torch.rand((256, V), generator=g4, device=dev).clamp_(1e-12, 1 - 1e-7)))
+        c4 = (torch.round(c4 * 16) / 16).float()
+        u4 = torch.rand(256, generator=g4, device=dev, dtype=torch.float64)
+        ms4 = timed(lambda: mxs_sampler.sample(c4, 1.0, 1024, u4, stream=stream), 5)
+        del c4
+        ties = {"bf16_rounded_k50": {"rows": rows, "ms_per_call_ids_only": ms16,
+                                     "rows_per_s_ids_only": rows / (ms16 / 1e3),
+                                     "ms_per_call_with_topk_order": ms16k},
+                "c4_gumbel_k1024": {"rows": 256, "ms_per_call": ms4, "rows_per_s": 256 / (ms4 / 1e3),
+                                    "workload": "256 x 151936 standard Gumbel quantised to 1/16, T=1.0, "
+                                                "top_k 1024, top-k order returned"}}
+
     vocab = None
     if world > 1 and not args.no_vocab:
         del logits
@@ -465,6 +505,8 @@ def main():
                              for r, v in enumerate(per_rank)]}
         if vocab is not None:
             line["vocab_sharded"] = vocab
+        if ties is not None:
+            line["tie_heavy"] = ties
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -298,25 +298,33 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
             float th;  // logits strictly above it pass
             if (t == 0) {
                 // The unit's first tile: the fast path's candidates, every logit
-                // >= a lower bound of the tile's k-th largest value (seeded from
-                // each lane's largest logits). Its would-enter logits are not
-                // listed: a replay reads the first tile again.
-                float m1 = -INFINITY, m2 = -INFINITY, m4 = -INFINITY;
-                if (k <= 64) {
-#pragma unroll
-                    for (int b = 0; b < 32; ++b) {
-                        if ((valid >> b) & 1u) {
-                            const float x = vv[b];
-                            if (x > m1) {
-                                m2 = m1;
-                                m1 = x;
-                            } else if (x > m2) {
-                                m2 = x;
-                            }
-                        }
-                    }
-                } else {
-                    float m3 = -INFINITY;
+                // >= a lower bound of the tile's k-th largest value, seeded from
+                // each lane's largest logit (the max tree's top). Its
+                // would-enter logits are not listed: a replay reads the first
+                // tile again.
+                const int nv = __popc(valid);
+                // lane maxima sorted: lanes 0..m-1 seed the top-m list; for
+                // k <= 32 the k-th is also this warp's own bound (k distinct
+                // logits are >= it).
+                const uint32_t sorted1 = warp_sort32_desc(nv >= 1 ? fkey(mxn) : 0u);
+                float seed = (k <= 32) ? bound_of(__shfl_sync(0xffffffffu, sorted1, k - 1)) : -INFINITY;
+                lkey = (lane < m) ? sorted1 : 0u;
+                publish(0);
+                // Once every consumer warp has published its first-tile m-th
+                // key, their minimum bounds the tile's k-th largest: 8m >= k
+                // distinct logits are at or above it.
+                csync();
+                uint32_t mn = 0xFFFFFFFFu;
+                if (lane < NWARPS) mn = (uint32_t)*reinterpret_cast<volatile uint64_t*>(&us.pubh[lane][0]);
+                mn = __reduce_min_sync(0xffffffffu, mn);
+                if (mn) {
+                    seed = fmaxf(seed, bound_of(mn));
+                } else if (k > 32) {
+                    // Some warp holds fewer than m logits of this tile (a short
+                    // row): this warp's own bound, the ceil(k/2)-th largest lane
+                    // second maximum (k <= 64) or the ceil(k/4)-th largest lane
+                    // fourth maximum (each such lane holds 2 or 4 logits >= it).
+                    float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY, m4 = -INFINITY;
                     for (int b = 0; b < 32; ++b) {
                         if ((valid >> b) & 1u) {
                             const float x = vv[b];
@@ -331,34 +339,16 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
                             }
                         }
                     }
+                    uint32_t own;
+                    if (k <= 64) {
+                        const uint32_t sorted2 = warp_sort32_desc(nv >= 2 ? fkey(m2) : 0u);
+                        own = __shfl_sync(0xffffffffu, sorted2, (k + 1) / 2 - 1);
+                    } else {
+                        const uint32_t sorted4 = warp_sort32_desc(nv >= 4 ? fkey(m4) : 0u);
+                        own = __shfl_sync(0xffffffffu, sorted4, (k + 3) / 4 - 1);
+                    }
+                    seed = bound_of(own);
                 }
-                const int nv = __popc(valid);
-                // lane maxima sorted: lanes 0..m-1 seed the top-m list; for
-                // k <= 32 the k-th is also this warp's own bound (k distinct
-                // logits are >= it). For k > 32: the ceil(k/2)-th largest lane
-                // second-maximum (each of those lanes holds two logits >= it).
-                const uint32_t sorted1 = warp_sort32_desc(nv >= 1 ? fkey(m1) : 0u);
-                uint32_t own;
-                if (k <= 32) {
-                    own = __shfl_sync(0xffffffffu, sorted1, k - 1);
-                } else if (k <= 64) {
-                    const uint32_t sorted2 = warp_sort32_desc(nv >= 2 ? fkey(m2) : 0u);
-                    own = __shfl_sync(0xffffffffu, sorted2, (k + 1) / 2 - 1);
-                } else {  // the ceil(k/4)-th largest lane 4th-maximum: 4 logits per such lane
-                    const uint32_t sorted4 = warp_sort32_desc(nv >= 4 ? fkey(m4) : 0u);
-                    own = __shfl_sync(0xffffffffu, sorted4, (k + 3) / 4 - 1);
-                }
-                float seed = bound_of(own);
-                lkey = (lane < m) ? sorted1 : 0u;
-                publish(0);
-                // Once every consumer warp has published its first-tile m-th
-                // key, their minimum bounds the tile's k-th largest: filter the
-                // first tile against it rather than this warp's own seed alone.
-                csync();
-                uint32_t mn = 0xFFFFFFFFu;
-                if (lane < NWARPS) mn = (uint32_t)*reinterpret_cast<volatile uint64_t*>(&us.pubh[lane][0]);
-                mn = __reduce_min_sync(0xffffffffu, mn);
-                if (mn) seed = fmaxf(seed, bound_of(mn));
                 // x >= seed as a strict test (a seed of -inf lets -inf through
                 // as "not above": a row whose k-th largest is -inf then has too
                 // few candidates and is replayed from its full logits)
