@@ -1284,7 +1284,9 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
         MXS_FIN_ADD(0, f1 - f0);
         MXS_FIN_ADD(6, cnt_all);
         bool tie = false;
-        if (!exact && cnt > k) {
+        if (!exact && cnt > (k <= 64 ? 64 : KSPLIT_K)) {
+            // more candidates than the smallest register sort for k takes:
+            // keep those >= the k-th
             const uint32_t kth = warp_select_kth_small(w.keys, cnt, k);
             cnt = warp_compact_ge(w.keys, w.idx, cnt, kth);
             if (cnt != k) {  // a tie straddles the cut
