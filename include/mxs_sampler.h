@@ -140,6 +140,27 @@ MXS_API int mxs_token_checks(int64_t rows, int top_k, int64_t vocab, const int32
                              const uint8_t* d_token_class, const uint8_t* d_first_step, uint8_t* d_stop,
                              void* stream);
 
+/*
+ * The output projection kept on the device, then mxs_sample_topk_ex: logits =
+ * hidden . weight^T (the reference's lm_head step, src/api/minxfmr.cpp:1918-2036
+ * and src/backend/cuda/cuda_backend.cu:731-780, whose logits it then copies to
+ * the host at :1440-1442), as a cuBLAS GEMM with bf16 operands and fp32
+ * accumulation and output, sampled where it lands in HBM.
+ *   d_hidden   rows x d_model bf16 (row r at d_hidden + r*ld_hidden elements)
+ *   d_weight   vocab x d_model bf16 (row v at d_weight + v*ld_weight elements)
+ *   d_logits_out  rows x ld_logits fp32 (nullable: a library-owned buffer with
+ *              a leading dimension rounded up to a multiple of 4)
+ * The sampled ids equal the reference block's on these logits (the GEMM is
+ * fp32-accumulated, not the reference's own dot-product order). cuBLAS is
+ * looked up at run time (MXS_ERR_CUDA when absent). Calls on one device run
+ * one at a time (a per-device lock).
+ */
+MXS_API int mxs_sample_from_hidden(const void* d_hidden, int64_t ld_hidden, const void* d_weight, int64_t ld_weight,
+                                   int64_t rows, int64_t d_model, int64_t vocab, double temperature, int top_k,
+                                   double top_p, double min_p, const double* d_u, int32_t* d_next,
+                                   int32_t* d_topk_idx, double* d_topk_prob, float* d_logits_out,
+                                   int64_t ld_logits, void* stream);
+
 /* Bytes of workspace mxs_sample_topk_ex needs for this shape on the current device. */
 MXS_API int mxs_workspace_size(int64_t rows, int64_t vocab, int top_k, size_t* bytes);
 

@@ -17,7 +17,7 @@ OUT_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(OUT_DIR, "libmxs.so")
 # phase-timer build (-DMXS_PROFILE) for kernel analysis; never loaded by the product path
 PROF_LIB = os.path.join(OUT_DIR, "libmxs_prof.so")
-SOURCES = ["mxs_sampler.cu", "mxs_stream.cu", "mxs_api.cu", "mxs_noalloc.cu", "mxs_multi.cu"]
+SOURCES = ["mxs_sampler.cu", "mxs_stream.cu", "mxs_api.cu", "mxs_noalloc.cu", "mxs_multi.cu", "mxs_hidden.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 COMPILE_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

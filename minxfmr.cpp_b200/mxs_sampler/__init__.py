@@ -41,7 +41,7 @@ EXPORTS = (
     "mxs_sample_topk_host", "mxs_shard_candidates", "mxs_merge_sample", "mxs_get_status",
     "mxs_version", "mxs_sample_topk_noalloc", "mxs_set_profile_events", "mxs_sample_rowsharded",
     "mxs_sample_vocabsharded", "mxs_set_test_hooks", "mxs_vocabsharded_stats", "mxs_sample_topk_edits",
-    "mxs_token_checks",
+    "mxs_token_checks", "mxs_sample_from_hidden",
 )
 
 _P = ctypes.c_void_p
@@ -67,6 +67,7 @@ _SIGS = {
     "mxs_set_test_hooks": [_I64, _I, _I],
     "mxs_vocabsharded_stats": [ctypes.POINTER(_I64), ctypes.POINTER(_I64)],
     "mxs_token_checks": [_I64, _I, _I64, _P, _P, _P, _P, _P, _P],
+    "mxs_sample_from_hidden": [_P, _I64, _P, _I64, _I64, _I64, _I64, _D, _I, _D, _D, _P, _P, _P, _P, _P, _I64, _P],
     "mxs_sample_topk_edits": [_P, _I64, _I64, _I64, _D, _I, _D, _D, _P, _I, _P, _I64, _P, _I, _D, _D, _D, _P, _P,
                               _P, _P, _P, _P],
 }
@@ -194,6 +195,34 @@ def sample_edits(logits, temperature, top_k, u, special=None, history=None, hist
     _check("mxs_sample_topk_edits", rc)
     if return_flags:
         return nxt, idx, prob, flags
+    return nxt, idx, prob
+
+
+def sample_from_hidden(hidden, weight, temperature, top_k, u, top_p=1.0, min_p=0.0, logits_out=None,
+                       return_topk=True, stream=None):
+    """The output projection on the device, then the sampler
+    (mxs_sample_from_hidden): hidden [rows, d] bf16, weight [vocab, d] bf16
+    (CUDA tensors, unit column stride). logits_out (optional) [rows, vocab]
+    fp32 receives the logits. Returns (next, topk_idx, topk_prob)."""
+    _need_cuda(hidden, "hidden", torch.bfloat16)
+    _need_cuda(weight, "weight", torch.bfloat16)
+    _need_cuda(u, "u", torch.float64)
+    rows, d = hidden.shape
+    vocab = weight.shape[0]
+    if weight.shape[1] != d or hidden.stride(1) != 1 or weight.stride(1) != 1:
+        raise ValueError("hidden [rows, d] and weight [vocab, d] with unit column stride")
+    k = k_use(int(top_k), vocab)
+    dev = hidden.device
+    nxt = torch.empty(rows, dtype=torch.int32, device=dev)
+    idx = torch.empty((rows, k), dtype=torch.int32, device=dev) if return_topk else None
+    prob = torch.empty((rows, k), dtype=torch.float64, device=dev) if return_topk else None
+    ldl = 0 if logits_out is None else logits_out.stride(0)
+    with torch.cuda.device(dev):
+        rc = load().mxs_sample_from_hidden(_ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0), rows, d,
+                                           vocab, float(temperature), int(top_k), float(top_p), float(min_p),
+                                           _ptr(u), _ptr(nxt), _ptr(idx), _ptr(prob), _ptr(logits_out), ldl,
+                                           _stream(stream))
+    _check("mxs_sample_from_hidden", rc)
     return nxt, idx, prob
 
 
