@@ -31,9 +31,27 @@ extern "C" __attribute__((visibility("default"))) int mxs_prof_read_stream(unsig
     }
     return 0;
 }
+// Phase clocks of row 0's finish (profiling build): sort + tie check, entry
+// writes, exps + sum, normalise, truncate + second sum, divide, cumulative
+// pick, calls.
+namespace mxs {
+__device__ unsigned long long g_draw_prof[8];
+}
+extern "C" __attribute__((visibility("default"))) int mxs_prof_read_draw(unsigned long long* host, int clear) {
+    if (cudaMemcpyFromSymbol(host, mxs::g_draw_prof, sizeof(mxs::g_draw_prof)) != cudaSuccess) return -3;
+    if (clear) {
+        static unsigned long long zeros[8];
+        if (cudaMemcpyToSymbol(mxs::g_draw_prof, zeros, sizeof(zeros)) != cudaSuccess) return -3;
+    }
+    return 0;
+}
+#define MXS_DRAW_T(v) long long v = clock64()
+#define MXS_DRAW_ADD(i, dt) do { if (row == 0 && (threadIdx.x & 31) == 0) atomicAdd(&g_draw_prof[i], (unsigned long long)(dt)); } while (0)
 #define MXS_SCLK(v) long long v = clock64()
 #define MXS_SADD(i, x) do { if (warp == 0) sclk[i] += (unsigned long long)(x); } while (0)
 #else
+#define MXS_DRAW_T(v) (void)0
+#define MXS_DRAW_ADD(i, x) (void)0
 #define MXS_SCLK(v) (void)0
 #define MXS_SADD(i, x) (void)0
 #endif
@@ -590,6 +608,7 @@ __device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, doub
     const double T = p.temperature;
     bool greedy = (T <= 0.0);
     double sum = 0.0;
+    MXS_DRAW_T(d0);
     if (!greedy) {
         const double maxs = dv ? dv[0] : (double)e[0].v;
         for (int i = lane; i < k; i += 32) pbuf[i] = exp(((dv ? dv[i] : (double)e[i].v) - maxs) / T);
@@ -598,6 +617,8 @@ __device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, doub
         sum = __shfl_sync(0xffffffffu, sum, 0);
         greedy = (sum <= 0.0);
     }
+    MXS_DRAW_T(d1);
+    MXS_DRAW_ADD(2, d1 - d0);
     if (greedy) {
         if (p.topk_prob)
             for (int i = lane; i < k; i += 32) p.topk_prob[row * k + i] = (i == 0) ? 1.0 : 0.0;
@@ -610,6 +631,8 @@ __device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, doub
         if (p.topk_prob) p.topk_prob[row * k + i] = q;
     }
     __syncwarp();
+    MXS_DRAW_T(d2);
+    MXS_DRAW_ADD(3, d2 - d1);
     int n = 0;
     double s2 = 0.0;
     if (lane == 0) {
@@ -619,17 +642,24 @@ __device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, doub
     n = __shfl_sync(0xffffffffu, n, 0);
     s2 = __shfl_sync(0xffffffffu, s2, 0);
     __syncwarp();
+    MXS_DRAW_T(d3);
+    MXS_DRAW_ADD(4, d3 - d2);
     if (n < 2) {  // discrete_distribution with fewer than two weights returns 0
         if (lane == 0) p.next[row] = e[0].i & COL_MASK;
         return 0;
     }
     for (int i = lane; i < n; i += 32) pbuf[i] = pbuf[i] / s2;
     __syncwarp();
+    MXS_DRAW_T(d4);
+    MXS_DRAW_ADD(5, d4 - d3);
     int pick = 0;
     if (lane == 0) {
         pick = cdf_pick(pbuf, n, p.u[row]);
         p.next[row] = e[pick].i & COL_MASK;
     }
+    MXS_DRAW_T(d5);
+    MXS_DRAW_ADD(6, d5 - d4);
+    MXS_DRAW_ADD(7, 1);
     return __shfl_sync(0xffffffffu, pick, 0);
 }
 
@@ -639,6 +669,7 @@ __device__ int warp_draw(const Params& p, int64_t row, const Ent* e, int k, doub
 template <int NS>
 __device__ __forceinline__ bool finish_sorted(const Params& p, int64_t row, FinishWarpSmem& w, int cnt, int k,
                                               bool tie, int lane) {
+    MXS_DRAW_T(s0);
     uint64_t b[NS];
 #pragma unroll
     for (int s2 = 0; s2 < NS; ++s2) {
@@ -665,6 +696,8 @@ __device__ __forceinline__ bool finish_sorted(const Params& p, int64_t row, Fini
 #pragma unroll
     for (int s2 = 0; s2 < NS; ++s2) any |= tm[s2];
     tie = tie || any != 0u;
+    MXS_DRAW_T(s1);
+    MXS_DRAW_ADD(0, s1 - s0);
     // With edited rows a key tie may hide an inexact double (bit 31): the
     // double replay resolves every tie there.
     if (tie && (p.topk_idx || p.edit_cnt)) return true;
@@ -681,6 +714,8 @@ __device__ __forceinline__ bool finish_sorted(const Params& p, int64_t row, Fini
             dv[i] = (w.e[i].i < 0) ? edit_value(p, row, w.e[i].i & COL_MASK) : (double)w.e[i].v;
         __syncwarp();
     }
+    MXS_DRAW_T(s2);
+    MXS_DRAW_ADD(1, s2 - s1);
     const int pick = warp_draw(p, row, w.e, k, w.pbuf, dv);
     uint32_t tp = 0u;
 #pragma unroll
