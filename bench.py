@@ -34,9 +34,9 @@ METRIC = "sampled rows/s (V=151936 fp32, top_k 50)"
 UNIT = "rows/s"
 # ncu dram__bytes_read.sum + dram__bytes_write.sum of one stream_select_kernel
 # launch per row of this workload, from an ncu capture of a 512-row launch of the
-# same kernel: 311,243,520 + 5,244,928 bytes / 512 rows. Traffic grows in
+# same kernel: 311,242,752 + 4,862,976 bytes / 512 rows. Traffic grows in
 # proportion to the rows, so it is scaled to a full launch.
-NCU_TRAFFIC_BYTES_PER_ROW = (311243520 + 5244928) / 512
+NCU_TRAFFIC_BYTES_PER_ROW = (311242752 + 4862976) / 512
 DOMINANT_KERNEL = "mxs::stream_select_kernel"
 
 
@@ -428,6 +428,46 @@ def main():
                "steps": n_e2e, "timing": "host wall clock around synchronous calls (max over ranks)"}
         del h_logits
 
+    # End to end from hidden states (f1, mxs_sample_from_hidden): host bf16
+    # hidden states [rows x 3584] in pinned memory, the output projection as a
+    # GEMM on the device against a bf16 weight [151,936 x 3584] resident in HBM,
+    # then the sampler; ids back to the host. A different workload from the
+    # headline (it includes the projection), so a sub-record of its own.
+    e2e_hidden = None
+    if not args.no_e2e:
+        D = 3584
+        gw = torch.Generator(device=dev)
+        gw.manual_seed(77 + rank)
+        weight = (torch.randn((V, D), generator=gw, device=dev) * (3.0 / D ** 0.5)).bfloat16()
+        h_hidden = torch.randn((rows, D), generator=gw, device=dev).bfloat16().cpu().pin_memory()
+        d_hidden = torch.empty((rows, D), dtype=torch.bfloat16, device=dev)
+        h_next = torch.empty(rows, dtype=torch.int32).pin_memory()
+
+        def hstep():
+            d_hidden.copy_(h_hidden, non_blocking=True)
+            n, _, _ = mxs_sampler.sample_from_hidden(d_hidden, weight, TEMPERATURE, TOP_K, u, return_topk=False,
+                                                     stream=stream)
+            h_next.copy_(n, non_blocking=True)
+            torch.cuda.synchronize()
+
+        for _ in range(2):
+            hstep()
+        if world > 1:
+            dist.barrier()
+        n_h = max(3, min(args.steps, 10))
+        t0 = time.perf_counter()
+        for _ in range(n_h):
+            hstep()
+        el = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(el, op=dist.ReduceOp.MAX)
+        e2e_hidden = {"value": world * rows * n_h / float(el.item()), "unit": UNIT,
+                      "h2d_bytes_per_step": rows * D * 2, "d2h_bytes_per_step": rows * 4, "steps": n_h,
+                      "workload": f"[{rows} x {D}] bf16 hidden states from pinned host memory -> bf16 GEMM with "
+                                  f"a [{V} x {D}] weight in HBM (cuBLAS, fp32 out) -> sampler (T=0.8, top_k 50) "
+                                  "-> ids to the host; host wall clock, max over ranks"}
+        del weight, d_hidden
+
     # Tie-heavy throughput (N = 1): the same rows rounded to bf16 (ties inside
     # nearly every row's top-k; every row takes the heap replay from its list),
     # and BASELINE's tie/large-k configuration (256 x 151,936 standard Gumbel
@@ -507,6 +547,8 @@ def main():
             line["vocab_sharded"] = vocab
         if ties is not None:
             line["tie_heavy"] = ties
+        if e2e_hidden is not None:
+            line["e2e_from_hidden"] = e2e_hidden
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
