@@ -36,6 +36,7 @@ def _nccl():
         lib.ncclGetUniqueId.argtypes = [ctypes.POINTER(_UniqueId)]
         lib.ncclCommInitRank.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _UniqueId, ctypes.c_int]
         lib.ncclCommDestroy.argtypes = [ctypes.c_void_p]
+        lib.ncclCommInitAll.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         lib.ncclCommCount.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
         lib.ncclGetErrorString.argtypes = [ctypes.c_int]
         lib.ncclGetErrorString.restype = ctypes.c_char_p
@@ -64,6 +65,16 @@ def comm_init_rank(world, uid, rank):
     comm = ctypes.c_void_p()
     _check("ncclCommInitRank", _nccl().ncclCommInitRank(ctypes.byref(comm), int(world), u, int(rank)))
     return comm.value
+
+
+def comm_init_all(devices):
+    """Communicators for several GPUs driven by one process (one per device,
+    rank i on devices[i]): for hosts that run one thread per GPU."""
+    n = len(devices)
+    comms = (ctypes.c_void_p * n)()
+    devs = (ctypes.c_int * n)(*devices)
+    _check("ncclCommInitAll", _nccl().ncclCommInitAll(comms, n, devs))
+    return [comms[i] for i in range(n)]
 
 
 def comm_count(comm):

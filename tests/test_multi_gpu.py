@@ -113,3 +113,47 @@ def test_bench_two_gpus_row_and_vocab_sharded():
     assert len(line["per_rank"]) == 2
     vs = line["vocab_sharded"]
     assert vs["shards"] == 2 and vs["parity_mismatch_rows"] == 0 and vs["value"] > 0
+
+
+THREADS = r'''
+import os, sys, json, threading, numpy as np, torch
+sys.path.insert(0, os.path.join(os.environ["ROOT"], "minxfmr.cpp_b200"))
+sys.path.insert(0, os.path.join(os.environ["ROOT"], "tests"))
+import workloads, oracle_lib, mxs_sampler
+from mxs_sampler import nccl
+world = 2
+rows, V, k, T = 32, 151936, 50, 0.8
+x = workloads.normal(91, rows, V, 2.0)
+x[3, 500:540] = 9.5  # a tie row: the list pass runs with both threads inside collectives
+u = oracle_lib.uniforms(91, rows)
+cols = V // world
+comms = nccl.comm_init_all(list(range(world)))
+out = [None] * world
+def rank_thread(r):
+    torch.cuda.set_device(r)
+    sh = torch.from_numpy(x[:, r * cols:(r + 1) * cols].copy()).cuda()
+    for _ in range(3):
+        n, i, p, f = mxs_sampler.sample_vocabsharded(sh, T, k, torch.from_numpy(u).cuda(), comms[r])
+    torch.cuda.synchronize()
+    out[r] = (n.cpu().numpy(), i.cpu().numpy())
+ts = [threading.Thread(target=rank_thread, args=(r,)) for r in range(world)]
+[t.start() for t in ts]
+[t.join() for t in ts]
+n0, i0, _ = oracle_lib.oracle_sample(x, T, k, u)
+ok = all(o is not None and (o[0] == n0).all() and (o[1] == i0).all() for o in out)
+for c in comms:
+    nccl.comm_destroy(c)
+print(json.dumps({"ok": bool(ok)}))
+sys.exit(0 if ok else 3)
+'''
+
+
+def test_vocab_sharded_one_thread_per_gpu():
+    """Two ranks driven by two threads of one process, each with its own
+    communicator (ncclCommInitAll): each call holds only its own device's lock
+    across its collectives, so the ranks never wait on each other's lock."""
+    _need_gpus(2)
+    env = dict(os.environ, ROOT=ROOT, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-c", THREADS], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, (r.stdout + r.stderr)[-3000:]
+    assert json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])["ok"]
