@@ -361,8 +361,10 @@ def main():
     def step():
         mxs_sampler.sample(logits, TEMPERATURE, TOP_K, u, out=out, return_topk=False, stream=stream)
 
+    t_host = time.perf_counter()
     for _ in range(args.warmup):
         step()
+    host_ms = (time.perf_counter() - t_host) * 1e3 / max(args.warmup, 1)  # host cost to queue one step
     torch.cuda.synchronize()
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES") else local
@@ -379,6 +381,12 @@ def main():
         torch.cuda.synchronize()
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
+        # A spin kernel holds the stream while the host queues the K steps, so
+        # the timed region is the device's back-to-back work: a rank whose host
+        # threads are slow to launch (eight ranks on a shared CPU) otherwise
+        # adds its launch gaps to the step time.
+        hold_ms = min(1000.0, 2.0 * host_ms * args.steps + 2.0)
+        torch.cuda._sleep(int(hold_ms * 1e-3 * 2.0e9))
         ev0.record(stream)
         for i in range(args.steps):
             step()
@@ -538,7 +546,8 @@ def main():
                 "config": {"workload": f"c5 throughput: [{rows} x {V}] fp32 logits per GPU, T=0.8, top_k 50, "
                                        "one uniform per row", "rows_per_gpu": rows, "vocab": V, "top_k": TOP_K,
                            "temperature": TEMPERATURE, "parallelism": f"row-sharded x{world}, no collective",
-                           "l2": "inputs (2.49 GB per GPU) larger than L2; no flush"},
+                           "l2": "inputs (2.49 GB per GPU) larger than L2; no flush",
+                           "launch": "steps queued behind a spin kernel; events time the device's back-to-back steps"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps,
                 "hbm_frac_of_8tbs": achieved / 8000.0, "clocks": clk.summary(),
                 "per_rank": [{"rank": r, "ms_per_step": v[0], "stream_kernel_ms": v[1]}
