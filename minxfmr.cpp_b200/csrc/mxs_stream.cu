@@ -31,7 +31,8 @@ extern "C" __attribute__((visibility("default"))) int mxs_prof_read_stream(unsig
     }
     return 0;
 }
-// Phase clocks of row 0's finish (profiling build): sort + tie check, entry
+// Phase clocks of the finish warps' draws, summed over rows (profiling build):
+// sort + tie check, entry
 // writes, exps + sum, normalise, truncate + second sum, divide, cumulative
 // pick, calls.
 namespace mxs {
@@ -46,7 +47,7 @@ extern "C" __attribute__((visibility("default"))) int mxs_prof_read_draw(unsigne
     return 0;
 }
 #define MXS_DRAW_T(v) long long v = clock64()
-#define MXS_DRAW_ADD(i, dt) do { if (row == 0 && (threadIdx.x & 31) == 0) atomicAdd(&g_draw_prof[i], (unsigned long long)(dt)); } while (0)
+#define MXS_DRAW_ADD(i, dt) do { if ((threadIdx.x & 31) == 0) atomicAdd(&g_draw_prof[i], (unsigned long long)(dt)); } while (0)
 #define MXS_SCLK(v) long long v = clock64()
 #define MXS_SADD(i, x) do { if (warp == 0) sclk[i] += (unsigned long long)(x); } while (0)
 #else
@@ -1089,11 +1090,14 @@ __device__ __forceinline__ uint32_t warp_select_kth_small(const uint32_t* keys, 
 }
 
 #ifdef MXS_PROFILE
-// Phase clocks of row 0's finish warp (profiling build): list, select, sort + draw,
-// list length, in-loop selections.
+// Phase clocks of the finish warps (profiling build), summed over rows: list,
+// select, sort + draw, wait for the streaming grid, whole row, rows, list
+// length; and a timeline in globaltimer ns: first CTA start, first and last
+// end of the wait, last CTA end.
 __device__ unsigned long long g_fin_prof[8];
+__device__ unsigned long long g_fin_tl[4];
 #define MXS_FIN_T(v) long long v = clock64()
-#define MXS_FIN_ADD(i, x) do { if (row == 0 && lane == 0) atomicAdd(&g_fin_prof[i], (unsigned long long)(x)); } while (0)
+#define MXS_FIN_ADD(i, x) do { if (lane == 0) atomicAdd(&g_fin_prof[i], (unsigned long long)(x)); } while (0)
 #else
 #define MXS_FIN_T(v) (void)0
 #define MXS_FIN_ADD(i, x) (void)0
@@ -1388,7 +1392,20 @@ __global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) 
     const int rpc = finish_rows_per_cta(p.rows);
     const int64_t row = warp < rpc ? (int64_t)blockIdx.x * rpc + warp : p.rows;  // p.rows: no row
     if (threadIdx.x == 0) s_xn = s_wn = 0;
+#ifdef MXS_PROFILE
+    const unsigned long long tl0 = (unsigned long long)globaltimer_ns();
+    const long long fw0 = clock64();
+#endif
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the streaming grid's lists are complete
+#ifdef MXS_PROFILE
+    const unsigned long long tl1 = (unsigned long long)globaltimer_ns();
+    if (threadIdx.x == 0) {
+        atomicMin(&g_fin_tl[0], tl0);
+        atomicMin(&g_fin_tl[1], tl1);
+        atomicMax(&g_fin_tl[2], tl1);
+    }
+    if (lane == 0 && row < p.rows) atomicAdd(&g_fin_prof[3], (unsigned long long)(clock64() - fw0));
+#endif
     MXS_PROF_BEGIN();
     csync();
     uint32_t flags = 0u, cnt_all = 0u;
@@ -1424,14 +1441,25 @@ __global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) 
     MXS_PROF_ADD(7, tx);
     MXS_PROF_COUNT(6, n);
     MXS_PROF_FLUSH();
+#ifdef MXS_PROFILE
+    if (lane == 0 && row < p.rows) {
+        atomicAdd(&g_fin_prof[4], (unsigned long long)(clock64() - fw0));
+        atomicAdd(&g_fin_prof[5], 1ull);
+    }
+    csync();
+    if (threadIdx.x == 0) atomicMax(&g_fin_tl[3], (unsigned long long)globaltimer_ns());
+#endif
 }
 
 #ifdef MXS_PROFILE
 extern "C" __attribute__((visibility("default"))) int mxs_prof_read_fin(unsigned long long* host, int clear) {
     if (cudaMemcpyFromSymbol(host, g_fin_prof, sizeof(g_fin_prof)) != cudaSuccess) return -3;
+    if (cudaMemcpyFromSymbol(host + 8, g_fin_tl, sizeof(g_fin_tl)) != cudaSuccess) return -3;
     if (clear) {
         static unsigned long long zeros[8];
+        static const unsigned long long tl[4] = {~0ull, ~0ull, 0ull, 0ull};
         if (cudaMemcpyToSymbol(g_fin_prof, zeros, sizeof(zeros)) != cudaSuccess) return -3;
+        if (cudaMemcpyToSymbol(g_fin_tl, tl, sizeof(tl)) != cudaSuccess) return -3;
     }
     return 0;
 }
