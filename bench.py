@@ -34,9 +34,9 @@ METRIC = "sampled rows/s (V=151936 fp32, top_k 50)"
 UNIT = "rows/s"
 # ncu dram__bytes_read.sum + dram__bytes_write.sum of one stream_select_kernel
 # launch per row of this workload, from an ncu capture of a 512-row launch of the
-# same kernel: 311,242,752 + 4,862,976 bytes / 512 rows. Traffic grows in
+# same kernel: 311,297,280 + 4,832,512 bytes / 512 rows. Traffic grows in
 # proportion to the rows, so it is scaled to a full launch.
-NCU_TRAFFIC_BYTES_PER_ROW = (311242752 + 4862976) / 512
+NCU_TRAFFIC_BYTES_PER_ROW = (311297280 + 4832512) / 512
 DOMINANT_KERNEL = "mxs::stream_select_kernel"
 
 
@@ -384,8 +384,9 @@ def main():
         # A spin kernel holds the stream while the host queues the K steps, so
         # the timed region is the device's back-to-back work: a rank whose host
         # threads are slow to launch (eight ranks on a shared CPU) otherwise
-        # adds its launch gaps to the step time.
-        hold_ms = min(1000.0, 2.0 * host_ms * args.steps + 2.0)
+        # adds its launch gaps to the step time. The hold is generous (a host
+        # thread descheduled for a few ms must not drain the queue).
+        hold_ms = min(2000.0, 4.0 * host_ms * args.steps + 200.0)
         torch.cuda._sleep(int(hold_ms * 1e-3 * 2.0e9))
         ev0.record(stream)
         for i in range(args.steps):

@@ -29,6 +29,7 @@ constexpr uint32_t FLAG_NAN = 2u;       // row holds a NaN logit
 constexpr uint32_t FLAG_OVERFLOW = 4u;  // candidate buffer overflowed (massive ties)
 constexpr uint32_t FLAG_TIMEOUT = 8u;   // a bounded wait gave up; outputs of the row are invalid
 constexpr uint32_t FLAG_UNSCANNED = 1u << 16;  // internal: row not streamed (k > KFAST), NaN state unknown
+constexpr uint32_t FLAG_DONE = 1u << 17;       // internal: row finished by the streaming kernel's idle warps
 
 // Order-preserving 32-bit key of a float: a > b (as floats, not NaN) iff
 // key(a) > key(b). -0.0 is folded into +0.0 first, since the reference compares

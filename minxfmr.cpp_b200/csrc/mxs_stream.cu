@@ -124,6 +124,11 @@ __device__ __forceinline__ uint32_t warp_sort32_desc(uint32_t v) {
     return v;
 }
 
+#ifndef MXS_EARLY_FINISH
+#define MXS_EARLY_FINISH 1
+#endif
+__device__ void finish_rows_early(const Params& p, unsigned char* smem, int64_t nj);
+
 __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
     extern __shared__ __align__(128) unsigned char smem[];
     float* ring = reinterpret_cast<float*>(smem);
@@ -544,6 +549,15 @@ __global__ void __launch_bounds__(NT_WS, 2) stream_select_kernel(Params p) {
         __syncwarp();
         MXS_SCLK(f2);
         MXS_SADD(5, f2 - f1);
+    }
+    // A CTA with one unit fewer than the busiest ones would idle for about a
+    // unit's streaming time until the grid completes: its consumer warps
+    // finish its own rows meanwhile (whole-row units only), so fewer are left
+    // to the finish kernel. Every tile this CTA loaded has been consumed, so
+    // the ring is free.
+    if (MXS_EARLY_FINISH && S == 1 && p.mode == MODE_SAMPLE && !p.edit_cnt && nj > 0 && nj < (p.units + G - 1) / G) {
+        csync();  // the CTA's rows are complete: lists, counts, flags, bounds
+        if (!*reinterpret_cast<volatile uint32_t*>(&sm.dead)) finish_rows_early(p, smem, nj);
     }
 #ifdef MXS_PROFILE
     if (warp == 0 && lane == 0) {
@@ -1269,12 +1283,26 @@ __global__ void __launch_bounds__(F_WARPS * 32) merge_rows_kernel(Params p) {
 
 // *out_full: the row's list cannot stand for it (NaN, overflow, fewer than k
 // candidates), so a replay must read the whole row.
+// EARLY (the streaming kernel's idle warps, finish_rows_early): a row that
+// needs a replay or timed out is left untouched for the finish kernel (its
+// outputs are rewritten there); any other row is finished and marked
+// FLAG_DONE, which the finish kernel clears and skips.
+template <bool EARLY>
 __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w, uint32_t* out_flags,
                                 uint32_t* out_cnt, bool* out_full) {
     const int lane = threadIdx.x & 31;
     MXS_FIN_T(f0);
     const int k = p.k_use;
     uint32_t flags = p.row_flag[row];
+    if (EARLY && (flags & FLAG_TIMEOUT)) return true;
+    if (!EARLY && (flags & FLAG_DONE)) {
+        __syncwarp();
+        if (lane == 0) p.row_flag[row] = 0u;  // left clear for the next call
+        *out_flags = 0u;
+        *out_cnt = 0u;
+        *out_full = false;
+        return false;
+    }
     const uint32_t cnt_all = p.row_cnt[row];
     bool exact = (flags & (FLAG_NAN | FLAG_OVERFLOW)) != 0 || cnt_all > (uint32_t)p.row_cap ||
                  cnt_all < (uint32_t)k;
@@ -1347,6 +1375,17 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
         MXS_FIN_T(f3);
         MXS_FIN_ADD(2, f3 - f2);
     }
+    if (EARLY) {
+        if (exact) return true;
+        __syncwarp();
+        if (lane == 0) {
+            if (p.row_flags) p.row_flags[row] = flags;
+            p.row_cnt[row] = 0u;
+            p.row_bound[row] = 0u;
+            p.row_flag[row] = FLAG_DONE;
+        }
+        return false;
+    }
     if (lane == 0) {
         if (flags & FLAG_TIMEOUT) {
             p.next[row] = -1;
@@ -1361,6 +1400,24 @@ __device__ bool finish_row_warp(const Params& p, int64_t row, FinishWarpSmem& w,
     *out_cnt = cnt_all;
     *out_full = full;
     return exact && !(flags & FLAG_TIMEOUT);
+}
+
+// The idle consumer warps of a streaming CTA (stream_select_kernel) finish up
+// to two rows each of the CTA's own rows, the last ones first; the ring holds
+// their FinishWarpSmem. Rows that need a replay are left to the finish kernel.
+constexpr int EARLY_ROWS_PER_WARP = 2;
+static_assert(sizeof(FinishWarpSmem) * NWARPS <= S_RING, "finish areas overlay the streaming ring");
+__device__ void finish_rows_early(const Params& p, unsigned char* smem, int64_t nj) {
+    const int warp = threadIdx.x >> 5;
+    FinishWarpSmem& w = reinterpret_cast<FinishWarpSmem*>(smem)[warp];
+    const int64_t lo = max((int64_t)0, nj - (int64_t)NWARPS * EARLY_ROWS_PER_WARP);
+    for (int64_t j = nj - 1 - warp; j >= lo; j -= NWARPS) {
+        const int64_t row = blockIdx.x + j * (int64_t)gridDim.x;
+        uint32_t flags, cnt_all;
+        bool full;
+        (void)finish_row_warp<true>(p, row, w, &flags, &cnt_all, &full);
+        __syncwarp();
+    }
 }
 
 // Rows of the exact replay need a whole CTA; the finish kernel's CTAs are
@@ -1410,7 +1467,7 @@ __global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) 
     csync();
     uint32_t flags = 0u, cnt_all = 0u;
     bool full = false;
-    const bool need = row < p.rows && finish_row_warp(p, row, w, &flags, &cnt_all, &full);
+    const bool need = row < p.rows && finish_row_warp<false>(p, row, w, &flags, &cnt_all, &full);
     if (p.edit_cnt) {
         // Edited rows: every replay in double by the row's own warp; a row
         // with a NaN is left without a draw (next = -1, MXS_ROW_NAN).

@@ -140,6 +140,33 @@ def test_bf16_rounded_rows_all_tied(mxs, k):
         assert ((got[3] & mxs.ROW_EXACT) != 0).mean() > 0.9
 
 
+@pytest.mark.parametrize("k", [8, 50])
+def test_rows_finished_by_idle_streaming_ctas(mxs, k):
+    """700 rows on 296 streaming CTAs: CTAs with one row fewer than the busiest
+    finish their own rows while the grid drains, marking them done for the
+    finish kernel; rows that need a replay (ties with a top-k list, a draw on
+    a tied position, NaN) stay with the finish kernel. Mixed rows, ids-only and
+    full-output calls, two calls in a row on the same workspace."""
+    rows = 700
+    x = workloads.normal(910 + k, rows, workloads.V_QWEN, 2.0)
+    x[::3] = torch.from_numpy(x[::3]).to(torch.bfloat16).float().numpy()  # tie rows
+    x[5, 777] = np.nan
+    x[400, 123] = np.nan
+    u = oracle_lib.uniforms(910 + k, rows)
+    n0, i0, p0 = oracle_lib.oracle_sample(x, 0.8, k, u)
+    lg = torch.from_numpy(x).cuda()
+    uu = torch.from_numpy(u).cuda()
+    for _ in range(2):
+        nxt = torch.empty(rows, dtype=torch.int32, device="cuda")
+        mxs.sample(lg, 0.8, k, uu, out=(nxt, None, None, None), return_topk=False)
+        torch.cuda.synchronize()
+        bad = np.nonzero(nxt.cpu().numpy() != n0)[0]
+        assert bad.size == 0, f"ids only: next differs on rows {bad[:10]}"
+        got = run_gpu(mxs, x, 0.8, k, u)
+        assert_parity(x, 0.8, k, u, got, name=f"early finish k={k}")
+        assert (got[3][[5, 400]] & mxs.ROW_NAN).all()
+
+
 def test_ragged_vocab_strided_and_unaligned(mxs):
     rng = np.random.default_rng(11)
     for V, ld, off in [(1, 1, 0), (2, 3, 0), (3, 3, 1), (7, 9, 2), (4097, 4101, 1), (10001, 10001, 3),
