@@ -169,8 +169,11 @@ __device__ __forceinline__ float heap_place_top(Ent* h, int len, Ent e) {
 // Offers list[0, n) in order to a heap without NaN; returns the root value.
 template <bool LOOKAHEAD>
 __device__ __forceinline__ float heap_offer_list_top(Ent* h, int len, const Ent* list, int n, float root) {
+    if (n <= 0) return root;
+    Ent nx = list[0];  // loaded ahead, as in pair_offer_list
     for (int i = 0; i < n; ++i) {
-        const Ent e = list[i];
+        const Ent e = nx;
+        if (i + 1 < n) nx = list[i + 1];
         if (before(e.v, root)) root = heap_place_top<LOOKAHEAD>(h, len, e);
     }
     return root;
@@ -223,10 +226,15 @@ __device__ __forceinline__ void pair_build(PairHeap hp, int len) {
     for (int p = len / 2; p >= 1; --p) pair_place(hp, p, len, hp.h[p]);
 }
 
-// Offers list[0, n) in order; returns the root value.
+// Offers list[0, n) in order; returns the root value. The next entry is
+// loaded before the current one is placed, so an offer that does not enter
+// costs a compare, not a load round trip (list and heap never overlap).
 __device__ __forceinline__ float pair_offer_list(PairHeap hp, int len, const Ent* list, int n, float root) {
+    if (n <= 0) return root;
+    Ent nx = list[0];
     for (int j = 0; j < n; ++j) {
-        const Ent e = list[j];
+        const Ent e = nx;
+        if (j + 1 < n) nx = list[j + 1];
         if (before(e.v, root)) root = pair_place(hp, 1, len, e);
     }
     return root;
