@@ -361,13 +361,22 @@ def main():
     def step():
         mxs_sampler.sample(logits, TEMPERATURE, TOP_K, u, out=out, return_topk=False, stream=stream)
 
-    t_host = time.perf_counter()
     for _ in range(args.warmup):
         step()
-    host_ms = (time.perf_counter() - t_host) * 1e3 / max(args.warmup, 1)  # host cost to queue one step
     torch.cuda.synchronize()
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    # The timed steps, captured as one graph. A captured call passes its own
+    # workspace (the library-owned one may be reallocated by later calls).
+    ws = mxs_sampler.make_workspace(rows, V, TOP_K, dev)
+    mxs_sampler.sample(logits, TEMPERATURE, TOP_K, u, out=out, return_topk=False, workspace=ws)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(args.steps):
+            mxs_sampler.sample(logits, TEMPERATURE, TOP_K, u, out=out, return_topk=False, workspace=ws)
+    graph.replay()  # one untimed replay: the graph's first launch uploads it
+    torch.cuda.synchronize()
     # device timing of the dominant kernel in every timed step (library hook)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     for a, b in kev:  # torch creates the CUDA events on their first record
@@ -381,16 +390,12 @@ def main():
         torch.cuda.synchronize()
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
-        # A spin kernel holds the stream while the host queues the K steps, so
-        # the timed region is the device's back-to-back work: a rank whose host
-        # threads are slow to launch (eight ranks on a shared CPU) otherwise
-        # adds its launch gaps to the step time. The hold is generous (a host
-        # thread descheduled for a few ms must not drain the queue).
-        hold_ms = min(2000.0, 4.0 * host_ms * args.steps + 200.0)
-        torch.cuda._sleep(int(hold_ms * 1e-3 * 2.0e9))
+        # The K timed steps run as one CUDA graph (captured above), replayed
+        # once: the timed region is the device's back-to-back work, with no
+        # host launch in it, so a rank whose host threads are slow to launch
+        # (eight ranks on a shared CPU) does not stretch its step time.
         ev0.record(stream)
-        for i in range(args.steps):
-            step()
+        graph.replay()
         ev1.record(stream)
         torch.cuda.synchronize()
         ms_total = ev0.elapsed_time(ev1)
@@ -548,7 +553,7 @@ def main():
                                        "one uniform per row", "rows_per_gpu": rows, "vocab": V, "top_k": TOP_K,
                            "temperature": TEMPERATURE, "parallelism": f"row-sharded x{world}, no collective",
                            "l2": "inputs (2.49 GB per GPU) larger than L2; no flush",
-                           "launch": "steps queued behind a spin kernel; events time the device's back-to-back steps"},
+                           "launch": "the K timed steps captured in one CUDA graph, replayed once between the events"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps,
                 "hbm_frac_of_8tbs": achieved / 8000.0, "clocks": clk.summary(),
                 "per_rank": [{"rank": r, "ms_per_step": v[0], "stream_kernel_ms": v[1]}

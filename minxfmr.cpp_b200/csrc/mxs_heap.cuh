@@ -125,6 +125,28 @@ __device__ __forceinline__ float heap_place_top1(Ent* h, int len, Ent e) {
     return root;
 }
 
+// The heap's loads and stores as explicit shared-memory accesses (32-bit
+// shared addresses): the heap functions are reached through non-inlined
+// replay functions that only see a generic pointer, and a generic access
+// costs more latency than a shared one on every level of the chain.
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ int4 pair_ld(uint32_t a) {
+    int4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ Ent ent_ld(uint32_t a) {
+    uint32_t v, i;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v), "=r"(i) : "r"(a) : "memory");
+    return Ent{__uint_as_float(v), (int32_t)i};
+}
+__device__ __forceinline__ void ent_st(uint32_t a, float v, int32_t i) {
+    asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(a), "r"(__float_as_uint(v)), "r"((uint32_t)i) : "memory");
+}
+
 // Two levels per step: for a lone thread replaying a row (latency-bound).
 __device__ __forceinline__ float heap_place_top2(Ent* h, int len, Ent e) {
     // Two levels per round: the children and the four grandchildren of the
@@ -166,6 +188,66 @@ __device__ __forceinline__ float heap_place_top(Ent* h, int len, Ent e) {
     return LOOKAHEAD ? heap_place_top2(h, len, e) : heap_place_top1(h, len, e);
 }
 
+// heap_place_top2 on a heap in shared memory, with explicit shared loads and
+// stores (the same steps).
+__device__ __forceinline__ float heap_place_top2_s(Ent* h, int len, Ent e) {
+    const uint32_t base = smem_addr(h);
+    auto ld = [&](int n) { return ent_ld(base + 8u * (uint32_t)n); };
+    int hole = 0;
+    float root = e.v;
+    for (;;) {
+        const int c = 2 * hole + 1;
+        if (c >= len) break;
+        const int gc = 2 * c + 1;
+        Ent l = ld(c), r = l, g0 = l, g1 = l, g2 = l, g3 = l;
+        if (c + 1 < len) r = ld(c + 1);
+        if (gc < len) g0 = ld(gc);
+        if (gc + 1 < len) g1 = ld(gc + 1);
+        if (gc + 2 < len) g2 = ld(gc + 2);
+        if (gc + 3 < len) g3 = ld(gc + 3);
+        const bool take_r = (c + 1 < len) && !before(r.v, l.v);
+        const Ent ch = take_r ? r : l;
+        if (before(ch.v, e.v)) break;
+        ent_st(base + 8u * (uint32_t)hole, ch.v, ch.i);
+        if (hole == 0) root = ch.v;
+        hole = c + (take_r ? 1 : 0);
+        const int c2 = 2 * hole + 1;
+        if (c2 >= len) break;
+        const Ent l2 = take_r ? g2 : g0, r2 = take_r ? g3 : g1;
+        const bool take_r2 = (c2 + 1 < len) && !before(r2.v, l2.v);
+        const Ent ch2 = take_r2 ? r2 : l2;
+        if (before(ch2.v, e.v)) break;
+        ent_st(base + 8u * (uint32_t)hole, ch2.v, ch2.i);
+        hole = c2 + (take_r2 ? 1 : 0);
+    }
+    ent_st(base + 8u * (uint32_t)hole, e.v, e.i);
+    return root;
+}
+
+// Offers list[0, n) in order to a heap without NaN, both in shared memory;
+// returns the root value.
+__device__ __forceinline__ float heap_offer_list_top_s(Ent* h, int len, const Ent* list, int n, float root) {
+    if (n <= 0) return root;
+    const uint32_t la = smem_addr(list);
+    Ent nx = ent_ld(la);
+    for (int i = 0; i < n; ++i) {
+        const Ent e = nx;
+        if (i + 1 < n) nx = ent_ld(la + 8u * (uint32_t)(i + 1));
+        if (before(e.v, root)) root = heap_place_top2_s(h, len, e);
+    }
+    return root;
+}
+
+// heap_sort_top<true> on a heap in shared memory.
+__device__ __forceinline__ void heap_sort_top_s(Ent* h, int len) {
+    while (len > 1) {
+        --len;
+        const Ent e = h[len];
+        h[len] = h[0];
+        heap_place_top2_s(h, len, e);
+    }
+}
+
 // Offers list[0, n) in order to a heap without NaN; returns the root value.
 template <bool LOOKAHEAD>
 __device__ __forceinline__ float heap_offer_list_top(Ent* h, int len, const Ent* list, int n, float root) {
@@ -197,27 +279,28 @@ __device__ __forceinline__ void heap_sort_top(Ent* h, int len) {
 // alignment. Heaps without NaN only; the results equal heap_build /
 // heap_place_top1 / heap_sort_top on the 0-based layout.
 struct PairHeap {
-    Ent* h;  // h[1 .. len]
+    Ent* h;  // h[1 .. len], in shared memory
 };
 
 // Place e at hole `hole` of the subtree below it, top-down; returns the value
-// left at `hole`.
+// left at `hole`. The heap is in shared memory.
 __device__ __forceinline__ float pair_place(PairHeap hp, int hole, int len, Ent e) {
     const int top = hole;
     float top_v = e.v;
+    const uint32_t base = smem_addr(hp.h);
     for (;;) {
         const int c = 2 * hole;
         if (c > len) break;
-        const int4 pr = *reinterpret_cast<const int4*>(hp.h + c);
+        const int4 pr = pair_ld(base + 8u * (uint32_t)c);
         const float lv = __int_as_float(pr.x), rv = __int_as_float(pr.z);
         const bool right = (c + 1 <= len) && !before(rv, lv);
         const float chv = right ? rv : lv;
         if (before(chv, e.v)) break;
-        hp.h[hole] = Ent{chv, right ? pr.w : pr.y};
+        ent_st(base + 8u * (uint32_t)hole, chv, right ? pr.w : pr.y);
         if (hole == top) top_v = chv;
         hole = c + (right ? 1 : 0);
     }
-    hp.h[hole] = e;
+    ent_st(base + 8u * (uint32_t)hole, e.v, e.i);
     return top_v;
 }
 
@@ -231,10 +314,11 @@ __device__ __forceinline__ void pair_build(PairHeap hp, int len) {
 // costs a compare, not a load round trip (list and heap never overlap).
 __device__ __forceinline__ float pair_offer_list(PairHeap hp, int len, const Ent* list, int n, float root) {
     if (n <= 0) return root;
-    Ent nx = list[0];
+    const uint32_t la = smem_addr(list);  // list in shared memory
+    Ent nx = ent_ld(la);
     for (int j = 0; j < n; ++j) {
         const Ent e = nx;
-        if (j + 1 < n) nx = list[j + 1];
+        if (j + 1 < n) nx = ent_ld(la + 8u * (uint32_t)(j + 1));
         if (before(e.v, root)) root = pair_place(hp, 1, len, e);
     }
     return root;

@@ -234,7 +234,8 @@ __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int na
                 if (tid == 0) {  // no NaN here: top-down replacements
                     float root = h[0].v;
                     for (int w2 = 0; w2 < NWARPS; ++w2)
-                        root = heap_offer_list_top<true>(h, k, xl + w2 * SLOT, sm.warp_tot[w2], root);
+                        root = SMALL ? heap_offer_list_top_s(h, k, xl + w2 * SLOT, sm.warp_tot[w2], root)
+                                     : heap_offer_list_top<true>(h, k, xl + w2 * SLOT, sm.warp_tot[w2], root);
                 }
                 csync();
                 MXS_PROF_ADD(1, tof);
@@ -253,6 +254,8 @@ __device__ __forceinline__ void exact_row_t(const Params& p, int64_t row, int na
     if (tid == 0) {
         if (nan_state)
             heap_sort(h, k);
+        else if (SMALL)
+            heap_sort_top_s(h, k);
         else
             heap_sort_top<true>(h, k);
     }
