@@ -24,7 +24,9 @@
 
 namespace mxs {
 
-struct Ent {
+// 8-byte aligned: the heap's shared-memory accesses move an entry as one
+// 8-byte (or a pair as one 16-byte) load or store.
+struct __align__(8) Ent {
     float v;
     int32_t i;
 };

@@ -1440,7 +1440,7 @@ __device__ __forceinline__ int finish_rows_per_cta(int64_t rows) {
 
 __global__ void __launch_bounds__(F_WARPS * 32, 3) finish_rows_kernel(Params p) {
     extern __shared__ __align__(128) unsigned char fsmem[];
-    __shared__ Ent s_heap[HEAP_SMEM_MAX];
+    __shared__ __align__(16) Ent s_heap[HEAP_SMEM_MAX];
     __shared__ int64_t s_xrow[F_WARPS];
     __shared__ uint32_t s_xflag[F_WARPS];
     __shared__ int s_xn, s_wn;
